@@ -1,0 +1,107 @@
+/*
+ * tt_attention.h - C ABI of the sm_100a (B200) BF16 causal attention forward.
+ *
+ * Plain C: raw device pointers, element strides and sizes, a CUDA stream passed as
+ * `void*` (a cudaStream_t / CUstream), and an integer status. No allocation happens
+ * behind these entry points: the caller owns O, LSE and the workspace.
+ *
+ * Each entry point names the reference interface it replaces (Tiny-transformer,
+ * paths relative to that project).
+ *
+ * Device selection: call with the device that owns the pointers current on the
+ * calling thread (cudaSetDevice, or a torch CUDAGuard), as for any CUDA library.
+ */
+#ifndef TT_ATTENTION_H_
+#define TT_ATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TT_ATTN_API __attribute__((visibility("default")))
+#else
+#define TT_ATTN_API
+#endif
+
+#define TT_ATTN_ABI_VERSION 1
+#define TT_ATTN_HEAD_DIM 64
+
+typedef enum tt_attn_status {
+  TT_ATTN_OK = 0,
+  TT_ATTN_BAD_ARG = 1,     /* invalid sizes, pointers or strides; nothing was launched */
+  TT_ATTN_UNSUPPORTED = 2, /* valid request this path cannot take (layout, device);
+                              nothing was launched: copy to an aligned contiguous layout */
+  TT_ATTN_LAUNCH_FAIL = 3, /* a CUDA call failed; tt_attn_last_error() has the CUDA message */
+  TT_ATTN_TIMEOUT = 4      /* a kernel wait ran out (see tt_attn_device_status) */
+} tt_attn_status;
+
+/*
+ * Causal attention forward, BF16 in / BF16 O / FP32 LSE, head_dim 64.
+ *
+ * Replaces the BF16 branch of `attention_forward(q, k, v, past_len, segment_ids)`
+ * (csrc/attention/attention.cu:32-159, declared in csrc/attention/attention.h:7-9,
+ * bound in csrc/attention/bindings.cpp:4-8), i.e. the kernels
+ * attention_bf16::forward<EVEN_TILES> (attention_forward_BF16_kernel.cuh:232-389) and
+ * decode_partial / decode_merge (attention_decode_BF16_kernel.cuh:45-128).
+ *
+ *   q        [batch, heads, q_len, 64]  bf16, element strides q_strides[4]
+ *   k, v     [batch, heads, kv_len, 64] bf16, element strides k_strides / v_strides
+ *            (prefix views of a larger KV cache are read in place)
+ *   past_len must equal kv_len - q_len; key j is visible to query row i iff j <= i + past_len.
+ *   kv_lens  optional device int32[batch] (q_len must be 1): key j is visible iff
+ *            j < kv_lens[b]; values are clamped to [0, kv_len]; 0 gives O = 0, LSE = -inf.
+ *   out      contiguous [batch, heads, q_len, 64] bf16
+ *   lse      contiguous [batch, heads, q_len] fp32, natural log
+ *   workspace / workspace_bytes: device scratch of at least
+ *            tt_attn_forward_workspace_size(...) bytes (may be NULL when that is 0).
+ *   stream   cudaStream_t the kernels are launched on; no host synchronisation.
+ *
+ * Layout requirements (else TT_ATTN_UNSUPPORTED): last stride 1, other strides positive
+ * multiples of 8 elements, base pointers 16-byte aligned.
+ */
+TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
+    const void* q, const int64_t* q_strides,
+    const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
+    int64_t past_len, const int32_t* kv_lens,
+    void* out, float* lse,
+    void* workspace, size_t workspace_bytes,
+    void* stream);
+
+/* Scratch bytes tt_attn_forward_bf16 needs for this shape (split-KV decode partials).
+ * Replaces the partials tensor the reference allocates (attention.cu:128-129).
+ * Returns 0 for shapes that need none, and for invalid shapes. */
+TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, int64_t q_len,
+                                                  int64_t kv_len);
+
+/* 1 when a [.., .., .., 64] bf16 operand at `ptr` with these element strides can be read
+ * in place; 0 when it must first be copied to aligned contiguous storage.
+ * Replaces the alignment decision of aligned_contiguous (attention.cu:20-29). */
+TT_ATTN_API int tt_attn_layout_supported(const void* ptr, const int64_t* strides);
+
+/* 1 when the current device can run the kernels (compute capability 10.x), else 0.
+ * Replaces the SM80 capability check (attention.cu:72-73). */
+TT_ATTN_API int tt_attn_device_supported(void);
+
+/* Reads (and, when clear != 0, resets) the current device's kernel status bits:
+ * bit 0 = a bounded wait inside a kernel ran out. Synchronises the device. */
+TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear);
+
+/* Human-readable name of a status code. */
+TT_ATTN_API const char* tt_attn_status_string(tt_attn_status status);
+
+/* Message for the last non-OK status returned on the calling thread ("" if none). */
+TT_ATTN_API const char* tt_attn_last_error(void);
+
+TT_ATTN_API int tt_attn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TT_ATTENTION_H_ */

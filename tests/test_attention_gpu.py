@@ -1,0 +1,443 @@
+"""GPU parity suite for the sm_100a attention forward (needs a B200).
+
+Port of the reference's CUDA test catalogue (Tiny-transformer tests/test_student_attention.py:89-448)
+onto this path, checked against the CPU oracle (oracle/attention_oracle.py):
+
+* vs the FP64 oracle with the reference tests' tolerances: O atol 2e-2 / rtol 3e-2,
+  LSE atol 2e-4 / rtol 2e-5 (test_student_attention.py:116-117);
+* vs the restated BF16 ``reference.attention`` with the acceptance bar of this port:
+  max |dO| <= 2e-2, mean |dO| <= 2e-3, LSE relative error <= 1e-3 (vs the FP64 LSE).
+
+Tile-boundary cases are widened from the reference's 64-row tiles to this kernel's 128-row query
+tiles, 128-key KV tiles and 64/128/256-key decode chunks. Everything calls through the native
+extension, which calls the C ABI (tt_attn_forward_bf16).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import attention_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+O_ATOL, O_RTOL = 2e-2, 3e-2
+LSE_ATOL, LSE_RTOL = 2e-4, 2e-5
+MAX_ABS, MEAN_ABS, LSE_REL = 2e-2, 2e-3, 1e-3
+
+
+@pytest.fixture(scope="module")
+def ext():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    if torch.cuda.get_device_capability()[0] != 10:
+        pytest.skip("needs an sm_100 GPU")
+    from tiny_transformer_b200.operators._extension import load_attention_extension
+    return load_attention_extension()
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(42)
+
+
+def _np(x):
+    return x.detach().float().cpu().numpy()
+
+
+def sdpa_reference(q, k, v, past_len):
+    """torch SDPA on aligned clones with the reference's lower-right causal mask
+    (reference.py:56-64): the GPU library comparator the reference tests also use."""
+    tq, tk = q.shape[2], k.shape[2]
+    mask = torch.from_numpy(oracle.causal_allowed(tq, tk, past_len)).to(q.device)
+    return F.scaled_dot_product_attention(q.clone(), k.clone(), v.clone(), attn_mask=mask)
+
+
+@torch.no_grad()
+def check_forward(ext, q, k, v, past_len=0, kv_lens=None, sdpa=True):
+    originals = [x.clone() for x in (q, k, v)]
+    out, lse = ext.attention_forward(q, k, v, past_len, None, kv_lens)
+    torch.cuda.current_stream().synchronize()
+    qn, kn, vn = _np(q), _np(k), _np(v)
+    if kv_lens is None:
+        ref_o, ref_lse = oracle.attention_fp64(qn, kn, vn, past_len)
+        bf_o = oracle.reference_attention_bf16(qn, kn, vn, past_len)
+    else:
+        lens = kv_lens.cpu().numpy()
+        ref_o, ref_lse = oracle.decode_with_kv_lens(qn, kn, vn, lens)
+        bf_o, _ = oracle.decode_with_kv_lens(qn, kn, vn, lens, oracle.reference_bf16_with_lse)
+    assert out.dtype == torch.bfloat16 and lse.dtype == torch.float32
+    assert tuple(lse.shape) == tuple(q.shape[:-1]) and tuple(out.shape) == tuple(q.shape)
+    assert out.is_contiguous()
+    o = out.float().cpu()
+    torch.testing.assert_close(o, torch.from_numpy(ref_o).float(), atol=O_ATOL, rtol=O_RTOL)
+    torch.testing.assert_close(lse.cpu(), torch.from_numpy(ref_lse).float(), atol=LSE_ATOL,
+                               rtol=LSE_RTOL)
+    diff = np.abs(o.numpy() - bf_o)
+    assert diff.max() <= MAX_ABS, f"max |dO| vs reference {diff.max()}"
+    assert diff.mean() <= MEAN_ABS, f"mean |dO| vs reference {diff.mean()}"
+    fin = np.isfinite(ref_lse)
+    rel = np.abs(lse.cpu().numpy()[fin] - ref_lse[fin]) / np.maximum(np.abs(ref_lse[fin]), 1.0)
+    assert rel.size == 0 or rel.max() <= LSE_REL
+    assert torch.isfinite(out).all()
+    for x, original in zip((q, k, v), originals):
+        torch.testing.assert_close(x, original, atol=0, rtol=0)
+    if sdpa and kv_lens is None:
+        torch.testing.assert_close(out, sdpa_reference(q, k, v, past_len), atol=O_ATOL, rtol=O_RTOL)
+    from tiny_transformer_b200.operators import student
+    public = student.attention(q, k, v, past_len, None, kv_lens)
+    torch.testing.assert_close(public, out, atol=0, rtol=0)
+    return out
+
+
+def test_golden_fixtures(ext, golden):
+    """Stored outputs of the reference's own reference.attention (tests/golden)."""
+    for name, case in golden.items():
+        dev = [torch.from_numpy(case[x].astype(np.int16)).view(torch.bfloat16).cuda()
+               for x in ("q", "k", "v")]
+        lens = case.get("kv_lens")
+        kv_lens = None if lens is None else torch.from_numpy(lens).cuda()
+        out, lse = ext.attention_forward(*dev, int(case["past_len"]), None, kv_lens)
+        ref = oracle.bf16_bits_to_f32(case["o"])
+        diff = np.abs(out.float().cpu().numpy() - ref)
+        assert diff.max() <= MAX_ABS and diff.mean() <= MEAN_ABS, name
+        torch.testing.assert_close(lse.double().cpu(), torch.from_numpy(case["lse64"]),
+                                   atol=LSE_ATOL, rtol=LSE_RTOL, msg=name)
+
+
+def test_tiles_tails_and_cache(ext):
+    # reference :135-149, widened to 128-row query / 128-key tiles.
+    for tq, tk in ((1, 1), (2, 2), (17, 17), (63, 63), (64, 64), (65, 65), (127, 127), (128, 128),
+                   (129, 129), (193, 193), (255, 255), (256, 256), (257, 257), (512, 512),
+                   (1, 513), (7, 127), (7, 128), (7, 129), (7, 193), (65, 193), (130, 385)):
+        q = torch.randn(2, 3, tq, 64, device="cuda", dtype=torch.bfloat16)
+        stores = [torch.full((2, 3, tk + 64, 64), float("nan"), device="cuda",
+                             dtype=torch.bfloat16) for _ in range(2)]
+        for store in stores:
+            store[:, :, :tk].normal_()
+        check_forward(ext, q, stores[0][:, :, :tk], stores[1][:, :, :tk], tk - tq)
+
+
+def test_feature_subtiles_and_full_output_rescale(ext):
+    # reference :151-165: one QK feature per probe, rising scores across KV tiles.
+    key_codes = torch.arange(257, device="cuda", dtype=torch.float32) / 64
+    feature_codes = (torch.arange(64, device="cuda", dtype=torch.float32) - 32) / 16
+    v = (key_codes[:, None] * feature_codes[None, :]).to(torch.bfloat16).view(1, 1, 257, 64)
+    for feature in (0, 15, 16, 31, 32, 47, 48, 63):
+        q = torch.zeros_like(v)
+        k = torch.zeros_like(v)
+        q[..., feature] = 4
+        k[..., feature] = (key_codes * 8).to(torch.bfloat16)
+        check_forward(ext, q, k, v)
+
+
+def test_full_tile_mask_boundary(ext):
+    # reference :167-189 with 128-row boundaries added.
+    for tq in (63, 64, 65, 127, 128, 129):
+        for past in (0, 30, 63, 64, 65, 126, 127, 128, 129):
+            tk = tq + past
+            q, k = [torch.zeros(1, 1, t, 64, device="cuda", dtype=torch.bfloat16) for t in (tq, tk)]
+            v = torch.zeros_like(k)
+            v[:, :, 31].fill_(64)
+            if tk > 127:
+                v[:, :, 127].fill_(-64)
+            v[:, :, -1].add_(32)
+            before = check_forward(ext, q, k, v, past)
+            changed = v.clone()
+            changed[:, :, past + 1:].add_(16)
+            after = check_forward(ext, q, k, changed, past)
+            torch.testing.assert_close(before[:, :, :1], after[:, :, :1], atol=0, rtol=0)
+
+
+def test_key_reduction_spans_tile(ext):
+    # reference :191-203: first/last key of every 16-key MMA step over two 128-key tiles + tail.
+    q = torch.zeros(1, 1, 64, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(1, 1, 257, 64, device="cuda", dtype=torch.bfloat16)
+    for key_index in list(range(0, 257, 16)) + list(range(15, 257, 16)) + [256]:
+        v = torch.zeros_like(k)
+        v[:, :, key_index, :32] = 64
+        v[:, :, key_index, 32:] = -64
+        check_forward(ext, q, k, v, 193)
+
+
+def test_full_width_kv_pipeline_poisoned_tails(ext):
+    # reference :205-222: NaN directly after Tk in the same allocation.
+    for tq, tk in ((2, 63), (2, 64), (2, 65), (64, 64), (63, 128), (64, 127), (64, 128),
+                   (64, 129), (128, 192), (129, 192), (65, 129), (129, 257), (128, 383),
+                   (200, 700)):
+        q = torch.randn(1, 1, tq, 64, device="cuda", dtype=torch.bfloat16)
+        stores = [torch.full((1, 1, tk + 64, 64), float("nan"), device="cuda",
+                             dtype=torch.bfloat16) for _ in range(2)]
+        for storage in stores:
+            storage[:, :, :tk].normal_()
+        k, v = [storage[:, :, :tk] for storage in stores]
+        assert k.is_contiguous() and v.is_contiguous()
+        check_forward(ext, q, k, v, tk - tq)
+
+
+@torch.no_grad()
+def test_even_tiles_match_causal_prefix_of_tail_path(ext):
+    # reference :224-242: appending one query/key must not change earlier rows.
+    for tq, tk in ((128, 128), (128, 256), (256, 384), (64, 128)):
+        q = torch.randn(2, 2, tq + 1, 64, device="cuda", dtype=torch.bfloat16)
+        k = torch.randn(2, 2, tk + 1, 64, device="cuda", dtype=torch.bfloat16)
+        v = torch.randn_like(k)
+        v[:, :, -1].fill_(64)
+        even = [x[:, :, :-1].contiguous() for x in (q, k, v)]
+        check_forward(ext, *even, past_len=tk - tq)
+        check_forward(ext, q, k, v, past_len=tk - tq)
+        full_o, full_lse = ext.attention_forward(*even, tk - tq, None)
+        tail_o, tail_lse = ext.attention_forward(q, k, v, tk - tq, None)
+        torch.testing.assert_close(full_o, tail_o[:, :, :tq], atol=O_ATOL, rtol=O_RTOL)
+        torch.testing.assert_close(full_lse, tail_lse[:, :, :tq], atol=LSE_ATOL, rtol=LSE_RTOL)
+
+
+def test_output_feature_and_head_order(ext):
+    # reference :244-257: uniform attention reproduces V exactly.
+    features = torch.arange(64, device="cuda", dtype=torch.bfloat16) / 8 - 4
+    offsets = torch.tensor([-24., -8., 8., 24.], device="cuda", dtype=torch.bfloat16).view(2, 2, 1, 1)
+    for tq in (2, 63, 64, 65, 127, 128, 129, 257):
+        q = torch.zeros(2, 2, tq, 64, device="cuda", dtype=torch.bfloat16)
+        k = torch.zeros_like(q)
+        v = (offsets + features).expand_as(q).contiguous()
+        actual = check_forward(ext, q, k, v)
+        torch.testing.assert_close(actual, v, atol=0, rtol=0)
+
+
+def test_causal_tile_order_and_pipeline_transitions(ext):
+    # reference :259-271: head offsets expose tiles written to the wrong (b, h).
+    for tq, tk in ((2, 2), (33, 33), (128, 128), (129, 129), (129, 161), (193, 225), (300, 650)):
+        q = torch.zeros(2, 3, tq, 64, device="cuda", dtype=torch.bfloat16)
+        k = torch.zeros(2, 3, tk, 64, device="cuda", dtype=torch.bfloat16)
+        offsets = torch.arange(6, device="cuda").view(2, 3, 1, 1) / 8
+        tokens = torch.arange(tk, device="cuda").view(1, 1, tk, 1) / 256
+        v = (offsets + tokens).expand(2, 3, tk, 64).to(torch.bfloat16).contiguous()
+        check_forward(ext, q, k, v, tk - tq)
+
+
+def test_unaligned_and_strided_views(ext):
+    # reference :273-287 plus cache-prefix views read in place.
+    for t in (65, 1):
+        count = 2 * 3 * 65 * 64
+        views = [torch.randn(count + 1, device="cuda", dtype=torch.bfloat16)[1:].view(2, 3, 65, 64)
+                 for _ in range(3)]
+        assert all(x.data_ptr() % 16 != 0 for x in views)
+        q = views[0][:, :, :t]
+        check_forward(ext, q, views[1], views[2], 65 - t)
+    views = [torch.randn(2, 3, 65, 128, device="cuda", dtype=torch.bfloat16)[..., ::2] for _ in range(3)]
+    check_forward(ext, *views)
+    views = [torch.randn(1, 1, 65, 64, device="cuda", dtype=torch.bfloat16).expand(2, 3, -1, -1)
+             for _ in range(3)]
+    check_forward(ext, *views)
+    # Row stride 128 elements (a [..., :64] view of a wider tensor): TMA / per-row bulk copies.
+    wide = [torch.randn(2, 3, 200, 128, device="cuda", dtype=torch.bfloat16)[..., :64] for _ in range(3)]
+    check_forward(ext, *wide)
+    check_forward(ext, wide[0][:, :, :1], wide[1], wide[2], 199)
+    # KV-cache prefix views of a [B, H, capacity, 64] cache, prefill chunk and decode.
+    cache = [torch.randn(2, 3, 512, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    for tq, tk in ((5, 300), (1, 300), (128, 384)):
+        q = torch.randn(2, 3, tq, 64, device="cuda", dtype=torch.bfloat16)
+        check_forward(ext, q, cache[0][:, :, :tk], cache[1][:, :, :tk], tk - tq)
+
+
+def test_decode_split_boundaries_and_rescaling(ext):
+    # reference :289-310, boundaries of 64/128/256-key chunks and long caches.
+    for tk in (1, 2, 7, 63, 64, 65, 127, 128, 129, 255, 256, 257, 511, 512, 513, 4095, 4096, 4097,
+               8192, 8193):
+        q = torch.randn(2, 3, 1, 64, device="cuda", dtype=torch.bfloat16)
+        k, v = [torch.randn(2, 3, tk, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+        check_forward(ext, q, k, v, tk - 1)
+    q = torch.ones(2, 3, 1, 64, device="cuda", dtype=torch.bfloat16)
+    k, v = [torch.randn(2, 3, 257, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    k[:, :, :128].fill_(-10)
+    k[:, :, 128:256].fill_(10)
+    check_forward(ext, q, k, v, 256)
+    q.zero_()
+    v.fill_(1)
+    actual = check_forward(ext, q, k, v, 256)
+    torch.testing.assert_close(actual, torch.ones_like(actual), atol=0, rtol=0)
+
+
+def test_exact_output_large_logits_and_causality(ext):
+    # reference :312-328.
+    q = torch.zeros(2, 3, 193, 64, device="cuda", dtype=torch.bfloat16)
+    k, v = torch.zeros_like(q), torch.ones_like(q)
+    actual = check_forward(ext, q, k, v)
+    torch.testing.assert_close(actual, v, atol=0, rtol=0)
+    q.fill_(10)
+    k.fill_(10)
+    v.normal_()
+    check_forward(ext, q, k, v)
+    q.normal_()
+    k.normal_()
+    before = check_forward(ext, q, k, v)
+    k[:, :, 129:].add_(4)
+    v[:, :, 129:].add_(4)
+    after = check_forward(ext, q, k, v)
+    torch.testing.assert_close(before[:, :, :129], after[:, :, :129], atol=0, rtol=0)
+
+
+@torch.no_grad()
+def test_partial_denominator_across_tiles_and_lanes(ext):
+    # reference :330-347.
+    lane_bias = torch.tensor([-1.5, 0., 1.25, 2.5], device="cuda")
+    block_bias = torch.tensor([-4., 3., -2., 6., 1.], device="cuda")
+    for tq, tk in ((2, 129), (63, 193), (65, 257), (129, 321), (1, 700)):
+        q = torch.zeros(1, 2, tq, 64, device="cuda", dtype=torch.bfloat16)
+        k = torch.zeros(1, 2, tk, 64, device="cuda", dtype=torch.bfloat16)
+        q[..., 0] = 8
+        key = torch.arange(tk, device="cuda")
+        owner = (key % 8) // 2
+        for head in range(2):
+            k[0, head, :, 0] = (block_bias[(key // 64) % 5] + lane_bias[(owner + head) % 4]).to(torch.bfloat16)
+        check_forward(ext, q, k, torch.randn_like(k), tk - tq)
+
+
+@torch.no_grad()
+def test_softmax_natural_lse(ext):
+    # reference :349-368: LSE = 2*key_value + ln(n) exactly representable setups.
+    for tq, tk in ((64, 127), (65, 193), (128, 255), (1, 300)):
+        for key_value in (-10., -0.5, 0.5, 10.):
+            q = torch.full((1, 2, tq, 64), 0.25, device="cuda", dtype=torch.bfloat16)
+            k = torch.full((1, 2, tk, 64), key_value, device="cuda", dtype=torch.bfloat16)
+            v = torch.ones_like(k)
+            check_forward(ext, q, k, v, tk - tq)
+            out, lse = ext.attention_forward(q, k, v, tk - tq)
+            torch.testing.assert_close(out, torch.ones_like(out), atol=0, rtol=0)
+            expected = 2 * key_value + torch.arange(tk - tq + 1, tk + 1, device="cuda").float().log()
+            torch.testing.assert_close(lse, expected.expand_as(lse), atol=LSE_ATOL, rtol=LSE_RTOL)
+
+
+@torch.no_grad()
+def test_current_stream_with_alignment_copies(ext):
+    # reference :370-389: work is ordered on the caller's current stream, no device sync.
+    for tq, tk in ((65, 65), (1, 257), (130, 130)):
+        inputs = [torch.zeros(2 * 3 * t * 64 + 1, device="cuda", dtype=torch.bfloat16)[1:].view(2, 3, t, 64)
+                  for t in (tq, tk, tk)]
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(10_000_000)
+            for x, value in zip(inputs, (0.25, 0.5, 2.0)):
+                x.fill_(value)
+            actual, lse = ext.attention_forward(*inputs, tk - tq)
+            actual, lse = actual.clone(), lse.clone()
+        stream.synchronize()
+        torch.testing.assert_close(actual, torch.full_like(actual, 2.0), atol=0, rtol=0)
+        expected_lse = 1.0 + torch.arange(tk - tq + 1, tk + 1, device="cuda").float().log()
+        torch.testing.assert_close(lse, expected_lse.expand_as(lse), atol=LSE_ATOL, rtol=LSE_RTOL)
+
+
+def test_validation(ext):
+    # reference :391-412 (same message fragments).
+    inputs = [torch.randn(2, 3, 7, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    ids = torch.zeros(2, 7, dtype=torch.long, device="cuda")
+    with pytest.raises(RuntimeError, match="segment_ids is not supported"):
+        ext.attention_forward(*inputs, 0, ids)
+    for dtype in (torch.float32, torch.bfloat16):
+        for index in range(3):
+            mixed = [x.to(dtype) for x in inputs]
+            mixed[index] = mixed[index].to(torch.bfloat16 if dtype == torch.float32 else torch.float32)
+            with pytest.raises(RuntimeError, match="same dtype"):
+                ext.attention_forward(*mixed)
+    with pytest.raises(RuntimeError, match="float32 attention is not provided"):
+        ext.attention_forward(*[x.float() for x in inputs])
+    # Expanded views reach the grid checks without allocating. With 128-row query tiles the
+    # reference's second shape fits the grid, so a taller one stands in for it.
+    for shape in ((2**31, 1, 1, 64), (2**17, 1, 128 * 2**14, 64)):
+        big = torch.zeros(1, 1, 1, 64, device="cuda", dtype=torch.bfloat16).expand(shape)
+        with pytest.raises(RuntimeError, match="grid limits"):
+            ext.attention_forward(big, big, big)
+    with pytest.raises(RuntimeError, match="head_dim=64"):
+        x = torch.zeros(1, 1, 4, 32, device="cuda", dtype=torch.bfloat16)
+        ext.attention_forward(x, x, x)
+    with pytest.raises(RuntimeError, match="Tk == past_len"):
+        ext.attention_forward(*inputs, 3)
+    with pytest.raises(RuntimeError, match="non-negative"):
+        ext.attention_forward(*inputs, -1)
+    with pytest.raises(RuntimeError, match="4D"):
+        ext.attention_forward(inputs[0][0], inputs[1][0], inputs[2][0])
+    with pytest.raises(RuntimeError, match="same device"):
+        ext.attention_forward(inputs[0], inputs[1].cpu(), inputs[2])
+    with pytest.raises(RuntimeError, match="kv_lens requires single-token"):
+        ext.attention_forward(*inputs, 0, None, torch.ones(2, dtype=torch.int32, device="cuda"))
+    q1 = torch.randn(2, 3, 1, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="shape \\[B\\]"):
+        ext.attention_forward(q1, q1, q1, 0, None, torch.ones(3, dtype=torch.int32, device="cuda"))
+    x = inputs[0].clone().requires_grad_()
+    with pytest.raises(RuntimeError, match="backward"):
+        ext.attention_forward(x, inputs[1], inputs[2])
+
+
+@torch.no_grad()
+def test_cuda_graph_replay(ext):
+    # reference :414-437: capture covers alignment copies, allocations and split-KV workspace.
+    for tq, tk in ((65, 193), (1, 193), (1, 3000), (200, 200)):
+        inputs = [torch.randn(2 * 3 * t * 64 + 1, device="cuda", dtype=torch.bfloat16)[1:].view(2, 3, t, 64)
+                  for t in (tq, tk, tk)]
+        expected = check_forward(ext, *inputs, past_len=tk - tq)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                _, expected_lse = ext.attention_forward(*inputs, tk - tq)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            actual, lse = ext.attention_forward(*inputs, tk - tq)
+        for _ in range(2):
+            actual.fill_(float("nan"))
+            lse.fill_(float("nan"))
+            graph.replay()
+            torch.testing.assert_close(actual, expected, atol=0, rtol=0)
+            torch.testing.assert_close(lse, expected_lse, atol=0, rtol=0)
+
+
+def test_rejects_sequence_index_overflow_before_copy(ext):
+    # reference :439-448.
+    seed = torch.zeros(1, 1, 1, 64, device="cuda", dtype=torch.bfloat16)
+    for tq, tk in ((2**31, 2**31), (2, 2**31), (65, 2**31 + 64)):
+        q = seed.expand(1, 1, tq, 64)
+        kv = seed.expand(1, 1, tk, 64)
+        with pytest.raises(RuntimeError, match="sequence lengths must fit int32"):
+            ext.attention_forward(q, kv, kv, tk - tq)
+
+
+# ----------------------------------------------------------------------------- kv_lens (new)
+def test_kv_lens_masks_beyond_length(ext):
+    """Key j visible iff j < kv_lens[b]: NaN-poisoned cache beyond each length, lengths on chunk
+    boundaries, 0 (O = 0, LSE = -inf) and > Tk (clamped)."""
+    tk = 1100
+    lens_list = [1, 63, 64, 65, 255, 256, 257, 1000, 1100, 0, 5000, 700]
+    B = len(lens_list)
+    q = torch.randn(B, 2, 1, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, 2, tk, 64, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    for b, L in enumerate(lens_list):
+        k[b, :, min(L, tk):] = float("nan")
+        v[b, :, min(L, tk):] = float("nan")
+    for dtype in (torch.int32, torch.int64):
+        lens = torch.tensor(lens_list, device="cuda", dtype=dtype)
+        out, lse = ext.attention_forward(q, k, v, tk - 1, None, lens)
+        torch.cuda.synchronize()
+        assert torch.isfinite(out).all()
+        assert (out[9] == 0).all() and torch.isinf(lse[9]).all() and (lse[9] < 0).all()
+        clean = [torch.nan_to_num(x, nan=0.0) for x in (k, v)]
+        check_forward(ext, q, clean[0], clean[1], tk - 1, kv_lens=lens)
+
+
+def test_kv_lens_matches_prefix_calls(ext):
+    """A row with kv_lens[b] = L equals the plain operator on the prefix [:L] (past_len = L-1)."""
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    lens = torch.randint(1, 3000, (6,), generator=gen)
+    q = torch.randn(6, 4, 1, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(6, 4, 3000, 64, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    out, lse = ext.attention_forward(q, k, v, 2999, None, lens.int().cuda())
+    for b in range(6):
+        L = int(lens[b])
+        ob, lb = ext.attention_forward(q[b:b + 1], k[b:b + 1, :, :L], v[b:b + 1, :, :L], L - 1)
+        torch.testing.assert_close(out[b:b + 1], ob, atol=1e-2, rtol=0)
+        torch.testing.assert_close(lse[b:b + 1], lb, atol=1e-5, rtol=1e-5)

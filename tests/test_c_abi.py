@@ -1,0 +1,99 @@
+"""The C ABI library loads, exports every declared symbol, and validates arguments before any
+CUDA call (runs without a GPU: no kernel is launched here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "tt_attention.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from tiny_transformer_b200.operators._extension import load_c_abi
+    return load_c_abi()
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return re.findall(r"TT_ATTN_API\s+[\w\s\*]+?\b(tt_attn_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "tt_attn_forward_bf16" in names
+    assert len(names) == len(set(names)) >= 8
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} missing from libtt_attention.so"
+
+
+def test_status_strings_and_version(lib):
+    assert lib.tt_attn_abi_version() == 1
+    for code, name in enumerate(["TT_ATTN_OK", "TT_ATTN_BAD_ARG", "TT_ATTN_UNSUPPORTED",
+                                 "TT_ATTN_LAUNCH_FAIL", "TT_ATTN_TIMEOUT"]):
+        assert lib.tt_attn_status_string(code).decode() == name
+
+
+def _strides(*s):
+    return (ctypes.c_int64 * 4)(*s)
+
+
+def _call(lib, *, q=16, k=16, v=16, out=16, lse=16, B=1, H=1, tq=4, tk=4, d=64, past=0,
+          lens=None, qs=None, ks=None, vs=None, ws=None, ws_bytes=0):
+    qs = qs or _strides(tq * 64 * H, tq * 64, 64, 1)
+    ks = ks or _strides(tk * 64 * H, tk * 64, 64, 1)
+    vs = vs or ks
+    return lib.tt_attn_forward_bf16(q, qs, k, ks, v, vs, B, H, tq, tk, d, past, lens, out, lse,
+                                    ws, ws_bytes, None)
+
+
+def _err(lib):
+    return lib.tt_attn_last_error().decode()
+
+
+@pytest.mark.parametrize("kwargs,fragment", [
+    (dict(q=None), "must not be NULL"),
+    (dict(out=None), "must not be NULL"),
+    (dict(d=32), "head_dim=64"),
+    (dict(B=0), "positive"),
+    (dict(tk=0), "positive"),
+    (dict(past=-1), "non-negative"),
+    (dict(past=1), "Tk == past_len"),
+    (dict(tq=5, tk=4, past=0), "Tk == past_len"),
+    (dict(tq=2**31, tk=2**31), "fit int32"),
+    (dict(tq=2, tk=2, lens=16), "kv_lens requires"),
+    (dict(B=2**31 - 1, H=2), "grid limits"),
+])
+def test_bad_arguments_rejected_before_cuda(lib, kwargs, fragment):
+    assert _call(lib, **kwargs) == 1  # TT_ATTN_BAD_ARG
+    assert fragment in _err(lib)
+
+
+def test_unsupported_layouts(lib):
+    # Unaligned base, non-unit inner stride, stride not a multiple of 8 elements.
+    assert _call(lib, q=18) == 2
+    assert "aligned" in _err(lib)
+    assert _call(lib, ks=_strides(512, 256, 128, 2)) == 2
+    assert _call(lib, ks=_strides(4 * 66, 4 * 66, 66, 1), H=1, B=2, tk=4, tq=4) == 2
+
+
+def test_workspace_and_layout_queries(lib):
+    # Decode with enough keys splits into several chunks and needs partials.
+    n = lib.tt_attn_forward_workspace_size(8, 12, 1, 512)
+    assert n > 0 and n % (66 * 4) == 0
+    assert lib.tt_attn_forward_workspace_size(8, 12, 1, 64) == 0   # one chunk per sequence
+    assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # prefill needs none
+    assert lib.tt_attn_forward_workspace_size(0, 12, 1, 512) == 0
+    # Missing workspace for a split decode is rejected.
+    assert _call(lib, B=8, H=12, tq=1, tk=512, past=511) == 1
+    assert "workspace" in _err(lib)
+    assert lib.tt_attn_layout_supported(16, _strides(4096, 4096, 64, 1)) == 1
+    assert lib.tt_attn_layout_supported(17, _strides(4096, 4096, 64, 1)) == 0
+    assert lib.tt_attn_layout_supported(16, _strides(4096, 4096, 64, 2)) == 0
+    assert lib.tt_attn_layout_supported(16, _strides(0, 4096, 64, 1)) == 0
+    assert lib.tt_attn_layout_supported(None, _strides(4096, 4096, 64, 1)) == 0

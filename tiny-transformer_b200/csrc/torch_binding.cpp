@@ -1,0 +1,150 @@
+// PyTorch extension `tt_attention_C`: the reference's native operator surface
+// (`attention_forward(q, k, v, past_len=0, segment_ids=None) -> (O, LSE)`, Tiny-transformer
+// csrc/attention/bindings.cpp:4-8, attention.cu:32-159) on top of the C ABI in
+// include/tt_attention.h. This file owns validation (same checks and message fragments as
+// csrc/attention/attention_common.h:9-87 and attention.cu:36-73), output / workspace
+// allocation through the caching allocator, and the layout decision; all device work goes
+// through tt_attn_forward_bf16 on the current stream.
+#include <torch/extension.h>
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/core/GradMode.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <cstdint>
+#include <limits>
+#include <optional>
+#include <tuple>
+
+#include "tt_attention.h"
+
+namespace {
+
+void check_tensors(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v) {
+  for (const auto* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->defined(), "attention inputs must be defined");
+    TORCH_CHECK(t->is_cuda(), "All inputs must be CUDA tensors");
+  }
+  for (const auto* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->device() == q.device(), "All inputs must be on the same device");
+    TORCH_CHECK(t->scalar_type() == at::kFloat || t->scalar_type() == at::kBFloat16,
+                "attention supports only float32 and bf16 inputs");
+    TORCH_CHECK(t->scalar_type() == q.scalar_type(), "q, k, v must have the same dtype");
+    TORCH_CHECK(t->layout() == at::kStrided, "All inputs must be strided tensors");
+  }
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "q, k, v must be a 4D tensor");
+  TORCH_CHECK(k.size(0) == q.size(0) && v.size(0) == q.size(0),
+              "q, k, v must have the same first dimension");
+  TORCH_CHECK(k.size(1) == q.size(1) && v.size(1) == q.size(1),
+              "q, k, v must have the same second dimension");
+  TORCH_CHECK(k.size(3) == q.size(3) && v.size(3) == q.size(3),
+              "q, k, v must have the same last dimension");
+  TORCH_CHECK(q.size(3) == TT_ATTN_HEAD_DIM, "attention currently supports only head_dim=64");
+  TORCH_CHECK(q.size(0) > 0 && q.size(1) > 0 && q.size(2) > 0 && k.size(2) > 0,
+              "attention batch, heads and sequence lengths must be positive");
+}
+
+void check_mask(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                int64_t past_len) {
+  TORCH_CHECK(past_len >= 0, "past_len must be non-negative");
+  TORCH_CHECK(v.size(2) == k.size(2), "k and v must have the same sequence length");
+  // Subtract instead of adding: past_len + Tq may overflow.
+  TORCH_CHECK(k.size(2) >= q.size(2) && past_len == k.size(2) - q.size(2),
+              "expected Tk == past_len + Tq");
+}
+
+bool readable_in_place(const torch::Tensor& x) {
+  const int64_t st[4] = {x.stride(0), x.stride(1), x.stride(2), x.stride(3)};
+  int64_t canon[4] = {st[0], st[1], st[2], st[3]};
+  // Size-1 dimensions are never stepped over; their stride does not matter.
+  const int64_t contiguous[3] = {x.size(1) * x.size(2) * x.size(3), x.size(2) * x.size(3),
+                                 x.size(3)};
+  for (int d = 0; d < 3; ++d)
+    if (x.size(d) == 1) canon[d] = contiguous[d];
+  return tt_attn_layout_supported(x.data_ptr(), canon) != 0;
+}
+
+// Same fallback as the reference's aligned_contiguous (attention.cu:20-29), taken only
+// when the TMA / bulk-copy path cannot read the view in place.
+torch::Tensor aligned_contiguous(torch::Tensor x) {
+  if (readable_in_place(x)) return x;
+  x = x.contiguous();
+  if (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 != 0) x = x.clone();
+  return x;
+}
+
+}  // namespace
+
+std::tuple<torch::Tensor, torch::Tensor> attention_forward(
+    torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t past_len,
+    std::optional<torch::Tensor> segment_ids, std::optional<torch::Tensor> kv_lens) {
+  check_tensors(q, k, v);
+  check_mask(q, k, v, past_len);
+  TORCH_CHECK(!(at::GradMode::is_enabled() &&
+                (q.requires_grad() || k.requires_grad() || v.requires_grad())),
+              "the sm_100a attention forward has no backward; "
+              "call it under torch.no_grad() or use inference tensors");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16,
+              "float32 attention is not provided by the sm_100a path; pass bf16 q, k, v");
+  TORCH_CHECK(!segment_ids.has_value(), "segment_ids is not supported for bf16 kernel");
+  const int64_t B = q.size(0), H = q.size(1), Tq = q.size(2), Tk = k.size(2);
+  const int64_t max_grid = std::numeric_limits<int32_t>::max();
+  const int64_t q_tiles = (Tq + 127) / 128;
+  // Divide before multiplying: B * H * tiles must fit grid.x.
+  TORCH_CHECK(q_tiles <= max_grid && B <= max_grid / q_tiles / H,
+              "attention shape exceeds the supported CUDA grid limits");
+  TORCH_CHECK(Tk <= std::numeric_limits<int32_t>::max(),
+              "bf16 attention sequence lengths must fit int32 (Tk <= INT32_MAX)");
+  if (kv_lens.has_value()) {
+    const auto& lens = *kv_lens;
+    TORCH_CHECK(lens.defined() && lens.is_cuda() && lens.device() == q.device(),
+                "kv_lens must be a CUDA tensor on the same device as q");
+    TORCH_CHECK(lens.scalar_type() == at::kInt || lens.scalar_type() == at::kLong,
+                "kv_lens must be int32 or int64");
+    TORCH_CHECK(lens.dim() == 1 && lens.size(0) == B, "kv_lens must have shape [B]");
+    TORCH_CHECK(Tq == 1, "kv_lens requires single-token decode (Tq == 1)");
+  }
+
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  const auto* props = at::cuda::getDeviceProperties(q.get_device());
+  TORCH_CHECK(props->major == 10,
+              "the bf16 attention kernels require an sm_100 GPU (compute capability 10.x); "
+              "found SM", props->major, props->minor);
+  auto stream = c10::cuda::getCurrentCUDAStream(q.get_device());
+
+  q = aligned_contiguous(q);
+  k = aligned_contiguous(k);
+  v = aligned_contiguous(v);
+  torch::Tensor lens32;
+  if (kv_lens.has_value()) lens32 = kv_lens->to(at::kInt).contiguous();
+
+  auto o = torch::empty({B, H, Tq, TT_ATTN_HEAD_DIM}, q.options());
+  auto lse = torch::empty({B, H, Tq}, q.options().dtype(at::kFloat));
+  const size_t ws_bytes = tt_attn_forward_workspace_size(B, H, Tq, Tk);
+  torch::Tensor ws;
+  if (ws_bytes > 0)
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
+
+  const int64_t qs[4] = {q.stride(0), q.stride(1), q.stride(2), q.stride(3)};
+  const int64_t ks[4] = {k.stride(0), k.stride(1), k.stride(2), k.stride(3)};
+  const int64_t vs[4] = {v.stride(0), v.stride(1), v.stride(2), v.stride(3)};
+  const tt_attn_status st = tt_attn_forward_bf16(
+      q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, B, H, Tq, Tk, TT_ATTN_HEAD_DIM,
+      past_len, lens32.defined() ? lens32.data_ptr<int32_t>() : nullptr, o.data_ptr(),
+      lse.data_ptr<float>(), ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes,
+      static_cast<void*>(stream.stream()));
+  TORCH_CHECK(st == TT_ATTN_OK, "tt_attn_forward_bf16 failed: ", tt_attn_status_string(st),
+              ": ", tt_attn_last_error());
+  return {o, lse};
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("attention_forward", &attention_forward,
+        "BF16 causal attention forward on sm_100a (returns O and natural-log FP32 LSE)",
+        pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"),
+        pybind11::arg("past_len") = 0, pybind11::arg("segment_ids") = pybind11::none(),
+        pybind11::arg("kv_lens") = pybind11::none());
+  m.attr("HEAD_DIM") = TT_ATTN_HEAD_DIM;
+  m.attr("ABI_VERSION") = TT_ATTN_ABI_VERSION;
+}

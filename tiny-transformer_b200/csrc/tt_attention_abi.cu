@@ -1,0 +1,340 @@
+// C-ABI implementation (include/tt_attention.h): argument validation, path selection
+// (split-KV decode for q_len == 1, tcgen05 prefill otherwise), TMA descriptor encoding
+// and kernel launches on the caller's stream. Nothing here allocates device memory.
+//
+// Reference host dispatcher this replaces: Tiny-transformer csrc/attention/attention.cu:32-159.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "tt_attention.h"
+#include "sm100_ptx.cuh"
+#include "prefill_sm100.cuh"
+#include "decode_sm100.cuh"
+
+namespace {
+
+constexpr float kScaleLog2 = 0.125f * 1.44269504088896340736f;  // (1/sqrt(64)) * log2(e)
+constexpr int kMaxDevices = 64;
+
+thread_local std::string g_last_error;
+
+tt_attn_status fail(tt_attn_status st, const std::string& msg) {
+  g_last_error = msg;
+  return st;
+}
+
+// ------------------------------------------------------------------ shape helpers
+struct Shape4 {
+  int64_t size[4];
+  int64_t stride[4];
+};
+
+// Strides of size-1 dimensions are never used to address memory; give them the
+// canonical contiguous value so stride checks and TMA descriptors accept them.
+Shape4 canonical(int64_t b, int64_t h, int64_t t, const int64_t* strides) {
+  Shape4 s{{b, h, t, TT_ATTN_HEAD_DIM}, {strides[0], strides[1], strides[2], strides[3]}};
+  const int64_t contiguous[3] = {h * t * TT_ATTN_HEAD_DIM, t * TT_ATTN_HEAD_DIM, TT_ATTN_HEAD_DIM};
+  for (int d = 0; d < 3; ++d)
+    if (s.size[d] == 1) s.stride[d] = contiguous[d];
+  return s;
+}
+
+bool strides_ok(const int64_t* st) {
+  if (st[3] != 1) return false;
+  for (int d = 0; d < 3; ++d)
+    if (st[d] <= 0 || st[d] % 8 != 0) return false;
+  return true;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Keys per decode CTA: the largest of 256/128/64 that still gives >= ~6 CTAs per SM.
+int decode_chunk(int64_t bh, int64_t tk) {
+  int chunk = tt::decode::MAX_CHUNK;
+  while (chunk > tt::decode::SUB && bh * ((tk + chunk - 1) / chunk) < 6 * 148) chunk /= 2;
+  return chunk;
+}
+
+// ------------------------------------------------------------------ driver entry point
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map over [B, H, T, 64] bf16 (dims listed innermost first), box 64 x 128 rows,
+// 128-byte swizzle; rows past T read as zero.
+bool encode_map(CUtensorMap* map, const void* base, const Shape4& s, std::string* err) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
+    return false;
+  }
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(s.size[3]), static_cast<cuuint64_t>(s.size[2]),
+                              static_cast<cuuint64_t>(s.size[1]), static_cast<cuuint64_t>(s.size[0])};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(s.stride[2]) * 2,
+                                 static_cast<cuuint64_t>(s.stride[1]) * 2,
+                                 static_cast<cuuint64_t>(s.stride[0]) * 2};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tt::prefill::BM), 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    *err = buf;
+    return false;
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ per-device setup
+struct DeviceState {
+  bool checked = false;
+  bool supported = false;
+  bool attrs_set = false;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+tt_attn_status prepare_device(int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TT_ATTN_UNSUPPORTED, "device index out of range");
+  *dev_out = dev;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceState& ds = g_dev[dev];
+  if (!ds.checked) {
+    int major = 0, minor = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+    ds.supported = (major == 10);
+    ds.checked = true;
+    if (!ds.supported) {
+      char buf[160];
+      std::snprintf(buf, sizeof(buf),
+                    "bf16 attention kernels require an sm_100 GPU (compute capability 10.x); "
+                    "device %d is SM%d%d",
+                    dev, major, minor);
+      g_last_error = buf;
+    }
+  }
+  if (!ds.supported) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf),
+                  "bf16 attention kernels require an sm_100 GPU (compute capability 10.x)");
+    return fail(TT_ATTN_UNSUPPORTED, buf);
+  }
+  if (!ds.attrs_set) {
+    e = cudaFuncSetAttribute(tt::prefill::attention_prefill_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(tt::prefill::kSmemBytes));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               2 * tt::decode::MAX_CHUNK * tt::decode::ROW_BYTES);
+    if (e != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    ds.attrs_set = true;
+  }
+  return TT_ATTN_OK;
+}
+
+tt_attn_status check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(TT_ATTN_LAUNCH_FAIL, std::string(what) + ": " + cudaGetErrorString(e));
+  return TT_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+TT_ATTN_API int tt_attn_abi_version(void) { return TT_ATTN_ABI_VERSION; }
+
+TT_ATTN_API const char* tt_attn_status_string(tt_attn_status status) {
+  switch (status) {
+    case TT_ATTN_OK: return "TT_ATTN_OK";
+    case TT_ATTN_BAD_ARG: return "TT_ATTN_BAD_ARG";
+    case TT_ATTN_UNSUPPORTED: return "TT_ATTN_UNSUPPORTED";
+    case TT_ATTN_LAUNCH_FAIL: return "TT_ATTN_LAUNCH_FAIL";
+    case TT_ATTN_TIMEOUT: return "TT_ATTN_TIMEOUT";
+  }
+  return "TT_ATTN_UNKNOWN";
+}
+
+TT_ATTN_API const char* tt_attn_last_error(void) { return g_last_error.c_str(); }
+
+TT_ATTN_API int tt_attn_layout_supported(const void* ptr, const int64_t* strides) {
+  if (ptr == nullptr || strides == nullptr) return 0;
+  return (aligned16(ptr) && strides_ok(strides)) ? 1 : 0;
+}
+
+TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, int64_t q_len,
+                                                  int64_t kv_len) {
+  if (batch <= 0 || heads <= 0 || q_len != 1 || kv_len <= 0 || kv_len > INT32_MAX) return 0;
+  const int64_t bh = batch * heads;
+  const int chunk = decode_chunk(bh, kv_len);
+  const int64_t n_chunks = (kv_len + chunk - 1) / chunk;
+  if (n_chunks <= 1) return 0;
+  return static_cast<size_t>(bh) * static_cast<size_t>(n_chunks) * tt::decode::PARTIAL *
+         sizeof(float);
+}
+
+TT_ATTN_API int tt_attn_device_supported(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+  return major == 10 ? 1 : 0;
+}
+
+TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear) {
+  if (flags == nullptr) return fail(TT_ATTN_BAD_ARG, "flags must not be NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(flags, tt::g_tt_status, sizeof(unsigned));
+  if (e == cudaSuccess && clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(tt::g_tt_status, &zero, sizeof(unsigned));
+  }
+  if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("status read: ") + cudaGetErrorString(e));
+  return (*flags & tt::TT_ERR_TIMEOUT) ? TT_ATTN_TIMEOUT : TT_ATTN_OK;
+}
+
+TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, int64_t batch, int64_t heads, int64_t q_len,
+    int64_t kv_len, int64_t head_dim, int64_t past_len, const int32_t* kv_lens, void* out,
+    float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+  // ---- validation: everything is checked before any CUDA call
+  if (!q || !k || !v || !out || !lse || !q_strides || !k_strides || !v_strides)
+    return fail(TT_ATTN_BAD_ARG, "q, k, v, out, lse and the stride arrays must not be NULL");
+  if (head_dim != TT_ATTN_HEAD_DIM)
+    return fail(TT_ATTN_BAD_ARG, "attention currently supports only head_dim=64");
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0)
+    return fail(TT_ATTN_BAD_ARG, "attention batch, heads and sequence lengths must be positive");
+  if (past_len < 0) return fail(TT_ATTN_BAD_ARG, "past_len must be non-negative");
+  if (kv_len < q_len || past_len != kv_len - q_len)
+    return fail(TT_ATTN_BAD_ARG, "expected Tk == past_len + Tq");
+  if (q_len > INT32_MAX || kv_len > INT32_MAX)
+    return fail(TT_ATTN_BAD_ARG, "bf16 attention sequence lengths must fit int32 (Tk <= INT32_MAX)");
+  if (kv_lens != nullptr && q_len != 1)
+    return fail(TT_ATTN_BAD_ARG, "kv_lens requires single-token decode (Tq == 1)");
+  if (batch > INT32_MAX / heads)
+    return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
+  const int64_t bh = batch * heads;
+  const bool is_decode = (q_len == 1);
+  int64_t grid = 0;
+  int chunk = 0;
+  int64_t n_chunks = 0;
+  if (is_decode) {
+    chunk = decode_chunk(bh, kv_len);
+    n_chunks = (kv_len + chunk - 1) / chunk;
+    if (n_chunks > INT32_MAX / bh)
+      return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
+    grid = bh * n_chunks;
+  } else {
+    const int64_t n_qtiles = (q_len + tt::prefill::BM - 1) / tt::prefill::BM;
+    if (n_qtiles > INT32_MAX / bh)
+      return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
+    grid = bh * n_qtiles;
+  }
+
+  const Shape4 qs = canonical(batch, heads, q_len, q_strides);
+  const Shape4 ks = canonical(batch, heads, kv_len, k_strides);
+  const Shape4 vs = canonical(batch, heads, kv_len, v_strides);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !strides_ok(qs.stride) ||
+      !strides_ok(ks.stride) || !strides_ok(vs.stride))
+    return fail(TT_ATTN_UNSUPPORTED,
+                "q/k/v need a unit last stride, other strides in multiples of 8 elements and "
+                "16-byte aligned bases; copy to aligned contiguous storage first");
+  if (!aligned16(out)) return fail(TT_ATTN_BAD_ARG, "out must be 16-byte aligned");
+  const size_t ws_needed = tt_attn_forward_workspace_size(batch, heads, q_len, kv_len);
+  if (ws_needed > 0 && (workspace == nullptr || workspace_bytes < ws_needed))
+    return fail(TT_ATTN_BAD_ARG, "workspace is smaller than tt_attn_forward_workspace_size()");
+
+  int dev = 0;
+  tt_attn_status st = prepare_device(&dev);
+  if (st != TT_ATTN_OK) return st;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+
+  if (is_decode) {
+    tt::decode::Params p{};
+    p.q = static_cast<const __nv_bfloat16*>(q);
+    p.k = static_cast<const __nv_bfloat16*>(k);
+    p.v = static_cast<const __nv_bfloat16*>(v);
+    p.q_sb = qs.stride[0];
+    p.q_sh = qs.stride[1];
+    p.k_sb = ks.stride[0];
+    p.k_sh = ks.stride[1];
+    p.k_st = ks.stride[2];
+    p.v_sb = vs.stride[0];
+    p.v_sh = vs.stride[1];
+    p.v_st = vs.stride[2];
+    p.kv_lens = kv_lens;
+    p.B = static_cast<int>(batch);
+    p.H = static_cast<int>(heads);
+    p.Tk = static_cast<int>(kv_len);
+    p.chunk = chunk;
+    p.n_chunks = static_cast<int>(n_chunks);
+    p.o = static_cast<__nv_bfloat16*>(out);
+    p.lse = lse;
+    p.partials = static_cast<float*>(workspace);
+    p.scale_log2 = kScaleLog2;
+    const size_t smem = 2u * static_cast<size_t>(chunk) * tt::decode::ROW_BYTES;
+    tt::decode::decode_split_kernel<<<static_cast<unsigned>(grid), tt::decode::THREADS, smem, cs>>>(p);
+    if ((st = check_launch("decode_split_kernel launch")) != TT_ATTN_OK) return st;
+    if (n_chunks > 1) {
+      tt::decode::decode_combine_kernel<<<static_cast<unsigned>(bh), tt::decode::HD, 0, cs>>>(p);
+      if ((st = check_launch("decode_combine_kernel launch")) != TT_ATTN_OK) return st;
+    }
+    return TT_ATTN_OK;
+  }
+
+  CUtensorMap tmq, tmk, tmv;
+  std::string err;
+  if (!encode_map(&tmq, q, qs, &err) || !encode_map(&tmk, k, ks, &err) ||
+      !encode_map(&tmv, v, vs, &err))
+    return fail(TT_ATTN_UNSUPPORTED, err);
+  tt::prefill::Params p{};
+  p.B = static_cast<int>(batch);
+  p.H = static_cast<int>(heads);
+  p.Tq = static_cast<int>(q_len);
+  p.Tk = static_cast<int>(kv_len);
+  p.past_len = static_cast<int>(past_len);
+  p.n_qtiles = static_cast<int>((q_len + tt::prefill::BM - 1) / tt::prefill::BM);
+  p.o = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  p.scale_log2 = kScaleLog2;
+  tt::prefill::attention_prefill_kernel<<<static_cast<unsigned>(grid), tt::prefill::THREADS,
+                                          tt::prefill::kSmemBytes, cs>>>(tmq, tmk, tmv, p);
+  return check_launch("attention_prefill_kernel launch");
+}
+
+}  // extern "C"
