@@ -15,6 +15,7 @@ rebuilt only when a source is newer than the output.
 from __future__ import annotations
 
 import os
+import re
 import subprocess
 import sys
 import sysconfig
@@ -54,10 +55,35 @@ def _stale(target: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _run(cmd: list[str], verbose: bool) -> None:
+def _run(cmd: list[str], verbose: bool) -> str:
     if verbose:
         print(" ".join(cmd), flush=True)
-    subprocess.run(cmd, check=True)
+    res = subprocess.run(cmd, check=True, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                         text=True)
+    if verbose and res.stdout.strip():
+        print(res.stdout, flush=True)
+    return res.stdout
+
+
+# The prefill kernel re-allocates registers between warpgroups (setmaxnreg); its launch register
+# count must equal the value that hand-over was sized for (prefill_sm100.cuh: LAUNCH_REGS).
+PREFILL_LAUNCH_REGS = 168
+
+
+def _check_ptxas(report: str) -> None:
+    lines = report.splitlines()
+    for i, line in enumerate(lines):
+        if "Compiling entry function" in line and "attention_prefill_kernel" in line:
+            for follow in lines[i + 1:i + 4]:
+                m = re.search(r"Used (\d+) registers", follow)
+                if m:
+                    regs = int(m.group(1))
+                    if regs != PREFILL_LAUNCH_REGS:
+                        raise RuntimeError(
+                            f"attention_prefill_kernel compiled with {regs} registers, expected "
+                            f"{PREFILL_LAUNCH_REGS}: the setmaxnreg hand-over would not be sound")
+                    return
+    raise RuntimeError("ptxas report for attention_prefill_kernel not found")
 
 
 def build_library(verbose: bool = False, force: bool = False) -> str:
@@ -68,12 +94,15 @@ def build_library(verbose: bool = False, force: bool = False) -> str:
         os.path.join(INCLUDE, "tt_attention.h")]
     out = lib_path()
     if force or _stale(out, deps):
-        cmd = [_nvcc(), *GENCODE, "-lineinfo", "-O3", "-std=c++17", "-shared",
+        cmd = [_nvcc(), *GENCODE, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xptxas=-v",
                "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I" + INCLUDE, "-I" + CSRC,
                *srcs, "-o", out, "-Xlinker", "-soname=" + LIB_NAME]
-        if verbose:
-            cmd.insert(1, "-Xptxas=-v")
-        _run(cmd, verbose)
+        try:
+            _check_ptxas(_run(cmd, verbose))
+        except Exception:
+            if os.path.exists(out):
+                os.remove(out)
+            raise
     return out
 
 

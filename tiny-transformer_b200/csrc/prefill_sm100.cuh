@@ -6,13 +6,19 @@
 //   softmax scale 1/sqrt(64), FP32 softmax, P rounded to BF16 before P.V,
 //   O in BF16, LSE = natural-log logsumexp of the scaled scores in FP32.
 //
-// One CTA computes one 128-row query tile of one (batch, head). Roles (6 warps):
-//   warps 0-3  softmax + epilogue: thread t owns query row t of the tile (TMEM lane t)
-//   warp  4    TMA producer: Q tile once, then K/V tiles through a STAGES-deep ring
-//   warp  5    tcgen05 issuer: S = Q.K^T (SS form) and O += P.V (TS form, P read from TMEM)
-// TMEM (256 columns): S in [0,128), P (bf16x2) in [128,192), O in [192,256).
-// Two CTAs fit on one SM (TMEM 2 x 256 columns, ~82 KB shared memory each), so one
-// CTA's softmax overlaps the other CTA's tensor-core work.
+// One CTA (one per SM) computes a 256-row query block of one (batch, head) as two 128-row
+// tiles t = 0, 1 that share every K/V tile the producer loads. Roles (3 warpgroups):
+//   warps 0-3   softmax + epilogue of tile 0 (thread = query row = TMEM lane)
+//   warps 4-7   softmax + epilogue of tile 1
+//   warp  8     TMA producer: Q tiles once, then K/V tiles through a STAGES-deep ring
+//   warps 9,10  tcgen05 issuers, one per query tile t: S_t(j+1) = Q_t.K(j+1)^T as soon as the
+//               softmax has read S_t(j), then O_t += P_t(j).V(j) (P from TMEM) once it publishes
+//               P_t(j). The tensor core computes the next scores while the softmax warps work
+//               on the current ones, and neither tile's issue order waits on the other tile.
+//   warp  11    idle (completes the third warpgroup for the register hand-over below)
+// Registers: launched at 168 per thread (384 threads, the 64K register file); the producer
+// warpgroup drops to 56 and the softmax warpgroups rise to 224 (2 x 224 + 56 = 504 <= 3 x 168).
+// TMEM (all 512 columns): S_t at [128t, 128t+128), P_t (bf16x2) at 256 + 64t, O_t at 384 + 64t.
 #pragma once
 
 #include <cuda.h>
@@ -25,28 +31,38 @@ namespace tt {
 namespace prefill {
 
 constexpr int BM = 128;                 // query rows per tile (UMMA M)
+constexpr int TILES = 2;                // query tiles per CTA
+constexpr int BLOCK_M = BM * TILES;     // query rows per CTA
 constexpr int BN = 128;                 // keys per KV tile (UMMA N of S)
 constexpr int HD = 64;                  // head dim
-constexpr int STAGES = 2;               // K/V ring depth
-constexpr int THREADS = 192;
-constexpr int LOAD_WARP = 4;
-constexpr int MMA_WARP = 5;
+constexpr int STAGES = 3;               // K/V ring depth
+constexpr int SOFTMAX_WARPS = 4 * TILES;
+constexpr int LOAD_WARP = SOFTMAX_WARPS;
+constexpr int MMA_WARP = SOFTMAX_WARPS + 1;  // MMA_WARP + t issues the MMAs of query tile t
+constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;  // three full warpgroups
+constexpr uint32_t LAUNCH_REGS = 168;    // registers per thread at launch (65536 / 384, rounded)
+constexpr uint32_t SOFTMAX_REGS = 224;
+constexpr uint32_t PRODUCER_REGS = 56;
+static_assert(2 * SOFTMAX_REGS + PRODUCER_REGS <= 3 * LAUNCH_REGS,
+              "register hand-over exceeds the launch allocation");
+static_assert(THREADS * LAUNCH_REGS <= 65536, "launch allocation exceeds the register file");
 constexpr uint32_t TILE_BYTES = BM * HD * 2;  // 16 KiB, one 128x64 bf16 tile
-constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t S_COL = 0, P_COL = 128, O_COL = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_COL = 0, P_COL = 256, O_COL = 384;
 constexpr float LN2 = 0.69314718055994530942f;
 // O is rescaled only when the running row max grows by more than this (log2 units);
 // between rescales P stays below 2^8, far inside the FP32/BF16 range.
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
 struct alignas(1024) Smem {
-  uint8_t q[TILE_BYTES];
+  uint8_t q[TILES][TILE_BYTES];
   uint8_t k[STAGES][TILE_BYTES];
   uint8_t v[STAGES][TILE_BYTES];
   uint64_t q_full;
   uint64_t k_full[STAGES], k_empty[STAGES];
   uint64_t v_full[STAGES], v_empty[STAGES];
-  uint64_t s_full, s_free, p_ready, pv_done, drain;
+  uint64_t s_full[TILES], s_free[TILES], p_ready[TILES], pv_done[TILES];
+  uint64_t drain[TILES];
   uint32_t tmem_base;
   volatile int abort;
 };
@@ -55,7 +71,7 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack for 1 KiB alignme
 
 struct Params {
   int B, H, Tq, Tk, past_len;
-  int n_qtiles;
+  int n_qblocks;     // ceil(Tq / BLOCK_M)
   __nv_bfloat16* o;  // contiguous [B, H, Tq, 64]
   float* lse;        // contiguous [B, H, Tq]
   float scale_log2;  // softmax scale * log2(e)
@@ -84,6 +100,96 @@ __device__ __forceinline__ bool warp_wait(Smem& s, uint64_t* bar, uint32_t parit
   return __all_sync(0xffffffffu, ok);
 }
 
+// Number of KV tiles query rows [q0, q0 + BM) need: keys up to q0 + BM - 1 + past_len.
+__device__ __forceinline__ int kv_tiles_for(const Params& p, int q0) {
+  if (q0 >= p.Tq) return 0;
+  const long long end =
+      min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + BM + p.past_len);
+  return static_cast<int>((end + BN - 1) / BN);
+}
+
+// Row maximum of the 128 scores: a 3-input max tree, depth ~6 instead of a 127-long chain.
+__device__ __forceinline__ float row_max(const float (&x)[BN]) {
+  float a[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = fmax3(x[i], x[i + 16], x[i + 32]);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = fmax3(a[i], x[i + 48], x[i + 64]);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = fmax3(a[i], x[i + 80], x[i + 96]);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = fmaxf(a[i], x[i + 112]);
+  float b[6];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) b[i] = fmax3(a[3 * i], a[3 * i + 1], a[3 * i + 2]);
+  b[5] = a[15];
+  return fmaxf(fmax3(b[0], b[1], b[2]), fmax3(b[3], b[4], b[5]));
+}
+
+// exp2 of two arguments on the FMA pipe, to take load off the MUFU unit (16 ex2 per clock
+// per SM, the binding limit of a D = 64 softmax). Cody-Waite range reduction
+// 2^x = 2^n * 2^f, n = round(x) by adding 1.5 * 2^23, f = x - n in [-1/2, 1/2]; 2^f by a
+// degree-3 minimax polynomial with p(0) = 1 (coefficients from fit_exp2_poly.py; maximum
+// relative error 1.02e-4 in FP32); n is added to the exponent field. Arguments are clamped
+// at -127, which yields exactly +0.0, so masked (-inf) scores give exact zeros.
+constexpr float kPolyC1 = 0.6932827f;    // 0x3f317afa
+constexpr float kPolyC2 = 0.24221104f;   // 0x3e78062c
+constexpr float kPolyC3 = 0.055009704f;  // 0x3d6151db
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+__device__ __forceinline__ void exp2_poly2(float a, float b, float& pa, float& pb) {
+  const uint64_t x2 = f2_pack(fmaxf(a, -127.f), fmaxf(b, -127.f));
+  const uint64_t t2 = f2_add(x2, f2_pack(kRoundMagic, kRoundMagic));
+  const uint64_t r2 = f2_add(t2, f2_pack(-kRoundMagic, -kRoundMagic));
+  const uint64_t f2 = f2_fma(r2, f2_pack(-1.f, -1.f), x2);
+  uint64_t p2 = f2_fma(f2_pack(kPolyC3, kPolyC3), f2, f2_pack(kPolyC2, kPolyC2));
+  p2 = f2_fma(p2, f2, f2_pack(kPolyC1, kPolyC1));
+  p2 = f2_fma(p2, f2, f2_pack(1.f, 1.f));
+  float q0, q1, n0, n1;
+  f2_unpack(p2, q0, q1);
+  f2_unpack(t2, n0, n1);
+  pa = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(n0) << 23));
+  pb = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(n1) << 23));
+}
+
+// Of every 8 consecutive score pairs, this many take the FMA-pipe exp2; the rest use MUFU.
+constexpr int POLY_PAIRS_PER_8 = 3;
+
+// p = exp2(x * sl2 - m) for the 128 scores of this row: packed f32x2 FMA for the argument,
+// MUFU ex2 (or the FMA-pipe polynomial for POLY_PAIRS_PER_8 of every 8 pairs), bf16x2
+// packing into `pk`, and the FP32 row sum over 8 independent packed accumulators. Returns
+// the row sum.
+__device__ __forceinline__ float exp_pack_sum(const float (&x)[BN], float sl2, float m,
+                                              uint32_t (&pk)[BN / 2]) {
+  const uint64_t sc2 = f2_pack(sl2, sl2);
+  const uint64_t nm2 = f2_pack(-m, -m);
+  uint64_t acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0;
+#pragma unroll
+  for (int c = 0; c < BN / 2; ++c) {
+    float t0, t1;
+    f2_unpack(f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2), t0, t1);
+    float p0, p1;
+    if ((c & 7) < POLY_PAIRS_PER_8) {
+      exp2_poly2(t0, t1, p0, p1);
+    } else {
+      p0 = ex2_approx(t0);
+      p1 = ex2_approx(t1);
+    }
+    acc[c & 7] = f2_add(acc[c & 7], f2_pack(p0, p1));
+    pk[c] = pack_bf16x2(p0, p1);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = f2_add(acc[i], acc[i + 4]);
+  acc[0] = f2_add(acc[0], acc[2]);
+  acc[1] = f2_add(acc[1], acc[3]);
+  acc[0] = f2_add(acc[0], acc[1]);
+  float lo, hi;
+  f2_unpack(acc[0], lo, hi);
+  return lo + hi;
+}
+
 __device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr,
                                             uint32_t idesc) {
   // K = 64 features = 4 UMMA k-steps of 16; each step advances 32 bytes inside the
@@ -107,7 +213,129 @@ __device__ __forceinline__ void issue_pv_mma(uint32_t tmem_o, uint32_t tmem_p, u
   }
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
+// Softmax + epilogue for query tile t (128 rows); executed by the 4 warps of that tile.
+__device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t tmem, int t,
+                                             int wq, int lane, int bh, int q0, int n_kv) {
+  const int r = wq * 32 + lane;  // query row within the tile == TMEM lane
+  const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+  const uint32_t t_s = tmem + lane_base + S_COL + t * BN;
+  const uint32_t t_p = tmem + lane_base + P_COL + t * (BN / 2);
+  const uint32_t t_o = tmem + lane_base + O_COL + t * HD;
+  const long long row_limit = static_cast<long long>(q0) + r + p.past_len;  // last visible key
+  const long long tile_limit = static_cast<long long>(q0) + p.past_len;     // row 0's limit
+  const float sl2 = p.scale_log2;
+  float m_run = -INFINITY;  // running max of scaled scores, log2 units
+  float l_run = 0.f;        // running sum of exp2(x - m_run)
+  bool ok = true;
+
+  for (int j = 0; j < n_kv; ++j) {
+    if (!warp_wait(s, &s.s_full[t], j & 1)) { ok = false; break; }
+    tc_fence_after();
+    float x[BN];
+    {
+      uint32_t raw[BN / 32][32];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_s + c * 32, raw[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        reg_fence(raw[c]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(raw[c][i]);
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.s_free[t]);
+
+    const long long kv0 = static_cast<long long>(j) * BN;
+    if (kv0 + BN - 1 > tile_limit) {
+#pragma unroll
+      for (int c = 0; c < BN; ++c)
+        if (kv0 + c > row_limit) x[c] = -INFINITY;
+    }
+    const float mx = row_max(x);
+    const float m_new = fmaxf(m_run, mx * sl2);
+    bool need = false;
+    float factor = 1.f;
+    if (j == 0) {
+      m_run = m_new;
+    } else if (m_new > m_run + RESCALE_THRESHOLD) {
+      need = true;
+      factor = ex2_approx(m_run - m_new);
+      m_run = m_new;
+    }
+    const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+    uint32_t pk[BN / 2];
+    const float rowsum = exp_pack_sum(x, sl2, m_use, pk);
+    l_run = l_run * factor + rowsum;
+
+    if (j > 0) {
+      // P_t and O_t are still in use by P.V of the previous KV tile until pv_done flips.
+      if (!warp_wait(s, &s.pv_done[t], (j - 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, need)) {
+        uint32_t o[HD / 32][32];
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          reg_fence(o[c]);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * factor);
+          tmem_st32(t_o + c * 32, o[c]);
+        }
+      }
+    }
+    {
+      uint32_t half[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) half[i] = pk[i];
+      tmem_st32(t_p, half);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) half[i] = pk[32 + i];
+      tmem_st32(t_p + 32, half);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.p_ready[t]);
+  }
+
+  if (ok && n_kv > 0 && warp_wait(s, &s.pv_done[t], (n_kv - 1) & 1)) {
+    tc_fence_after();
+    const int row = q0 + r;
+    const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+    uint32_t o[HD / 32][32];
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
+    tmem_wait_ld();
+    if (row < p.Tq) {
+      __nv_bfloat16* orow =
+          p.o + (static_cast<size_t>(bh) * p.Tq + static_cast<size_t>(row)) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        reg_fence(o[c]);
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          packed[i] = pack_bf16x2(__uint_as_float(o[c][2 * i]) * inv_l,
+                                  __uint_as_float(o[c][2 * i + 1]) * inv_l);
+        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                              packed[4 * i + 3]);
+      }
+      p.lse[static_cast<size_t>(bh) * p.Tq + row] =
+          l_run > 0.f ? (m_run + log2f(l_run)) * LN2 : -INFINITY;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
 attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -117,30 +345,36 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Heaviest causal tiles first: blocks are dispatched roughly in index order.
+  // Heaviest causal blocks first: blocks are dispatched roughly in index order.
   const int BH = p.B * p.H;
-  const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x / BH);
+  const int qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.x / BH);
   const int bh = static_cast<int>(blockIdx.x % BH);
   const int b = bh / p.H;
   const int h = bh % p.H;
-  const int q0 = qt * BM;
-  const long long kv_end_ll =
-      min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + BM + p.past_len);
-  const int n_kv = static_cast<int>((kv_end_ll + BN - 1) / BN);
+  int q0[TILES], n_kv[TILES];
+#pragma unroll
+  for (int t = 0; t < TILES; ++t) {
+    q0[t] = qb * BLOCK_M + t * BM;
+    n_kv[t] = kv_tiles_for(p, q0[t]);
+  }
+  // Tile 1 never needs fewer KV tiles than tile 0 unless it lies past Tq (then it needs none).
+  const int n_load = max(n_kv[0], n_kv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.k_full[i], 1);
-      mbar_init(&s.k_empty[i], 1);
+      mbar_init(&s.k_empty[i], TILES);  // released by both tiles' issuers
       mbar_init(&s.v_full[i], 1);
-      mbar_init(&s.v_empty[i], 1);
+      mbar_init(&s.v_empty[i], TILES);
     }
-    mbar_init(&s.s_full, 1);
-    mbar_init(&s.s_free, 4);
-    mbar_init(&s.p_ready, 4);
-    mbar_init(&s.pv_done, 1);
-    mbar_init(&s.drain, 1);
+    for (int t = 0; t < TILES; ++t) {
+      mbar_init(&s.s_full[t], 1);
+      mbar_init(&s.s_free[t], 4);
+      mbar_init(&s.p_ready[t], 4);
+      mbar_init(&s.pv_done[t], 1);
+      mbar_init(&s.drain[t], 1);
+    }
     s.abort = 0;
     fence_barrier_init();
   }
@@ -158,12 +392,15 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  if (warp == LOAD_WARP) {
-    if (lane == 0) {
+  if (warp >= SOFTMAX_WARPS) {
+    // Producer warpgroup: give registers to the softmax warpgroups, then split by warp.
+    regs_decrease<PRODUCER_REGS>();
+    if (warp == LOAD_WARP && lane == 0) {
       int issued_k = 0, issued_v = 0;  // K / V tiles whose loads were issued
-      mbar_arrive_expect_tx(&s.q_full, TILE_BYTES);
-      tma_load_4d(s.q, &tm_q, &s.q_full, 0, q0, h, b);
-      for (int j = 0; j < n_kv; ++j) {
+      const int q_tiles = n_kv[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(&s.q_full, q_tiles * TILE_BYTES);
+      for (int t = 0; t < q_tiles; ++t) tma_load_4d(s.q[t], &tm_q, &s.q_full, 0, q0[t], h, b);
+      for (int j = 0; j < n_load; ++j) {
         const int st = j % STAGES;
         const uint32_t use = j / STAGES;
         if (j >= STAGES && !wait_or_abort(s, &s.k_empty[st], (use - 1) & 1)) break;
@@ -183,169 +420,61 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int j = max(0, issued_v - STAGES); j < issued_v; ++j)
           mbar_wait(&s.v_full[j % STAGES], (j / STAGES) & 1);
       }
-    }
-  } else if (warp == MMA_WARP) {
-    if (lane == 0) {
+    } else if (warp >= MMA_WARP && warp < MMA_WARP + TILES && lane == 0) {
+      const int t = warp - MMA_WARP;
+      const int n = n_kv[t];
       const uint32_t idesc_s = make_idesc_bf16(BM, BN, false);
       const uint32_t idesc_o = make_idesc_bf16(BM, HD, true);
-      const uint32_t q_addr = smem_u32(s.q);
-      bool ok = wait_or_abort(s, &s.q_full, 0) && wait_or_abort(s, &s.k_full[0], 0);
-      if (ok) {
-        tc_fence_after();
-        issue_s_mma(tmem + S_COL, q_addr, smem_u32(s.k[0]), idesc_s);
-        umma_commit(&s.s_full);
-        umma_commit(&s.k_empty[0]);
+      const uint32_t q_addr = smem_u32(s.q[t]);
+      const uint32_t t_s = tmem + S_COL + t * BN;
+      const uint32_t t_p = tmem + P_COL + t * (BN / 2);
+      const uint32_t t_o = tmem + O_COL + t * HD;
+      bool ok = true;
+      if (n > 0) {
+        ok = wait_or_abort(s, &s.q_full, 0) && wait_or_abort(s, &s.k_full[0], 0);
+        if (ok) {
+          tc_fence_after();
+          issue_s_mma(t_s, q_addr, smem_u32(s.k[0]), idesc_s);
+          umma_commit(&s.s_full[t]);
+          umma_commit(&s.k_empty[0]);
+        }
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv) {
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) {
           const int st1 = (j + 1) % STAGES;
           if (!wait_or_abort(s, &s.k_full[st1], ((j + 1) / STAGES) & 1)) break;
-          if (!wait_or_abort(s, &s.s_free, j & 1)) break;
+          if (!wait_or_abort(s, &s.s_free[t], j & 1)) break;
           tc_fence_after();
-          issue_s_mma(tmem + S_COL, q_addr, smem_u32(s.k[st1]), idesc_s);
-          umma_commit(&s.s_full);
+          issue_s_mma(t_s, q_addr, smem_u32(s.k[st1]), idesc_s);
+          umma_commit(&s.s_full[t]);
           umma_commit(&s.k_empty[st1]);
         }
         const int st = j % STAGES;
-        if (!wait_or_abort(s, &s.p_ready, j & 1)) break;
         if (!wait_or_abort(s, &s.v_full[st], (j / STAGES) & 1)) break;
+        if (!wait_or_abort(s, &s.p_ready[t], j & 1)) break;
         tc_fence_after();
-        issue_pv_mma(tmem + O_COL, tmem + P_COL, smem_u32(s.v[st]), idesc_o, j > 0);
-        umma_commit(&s.pv_done);
+        issue_pv_mma(t_o, t_p, smem_u32(s.v[st]), idesc_o, j > 0);
+        umma_commit(&s.pv_done[t]);
         umma_commit(&s.v_empty[st]);
       }
+      // KV tiles this query tile does not need (the other tile still does): release each
+      // stage once it has been filled, so the producer's count of two releases per use holds.
+      for (int j = n; j < n_load && !s.abort; ++j) {
+        const int st = j % STAGES;
+        const uint32_t par = (j / STAGES) & 1;
+        if (!wait_or_abort(s, &s.k_full[st], par)) break;
+        mbar_arrive(&s.k_empty[st]);
+        if (!wait_or_abort(s, &s.v_full[st], par)) break;
+        mbar_arrive(&s.v_empty[st]);
+      }
       // All MMAs issued by this thread have completed once `drain` flips.
-      umma_commit(&s.drain);
-      mbar_wait(&s.drain, 0);
+      umma_commit(&s.drain[t]);
+      mbar_wait(&s.drain[t], 0);
     }
   } else {
-    // ---------------------------------------------------------------- softmax warps
-    const int r = warp * 32 + lane;  // query row within the tile == TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t t_s = tmem + lane_base + S_COL;
-    const uint32_t t_p = tmem + lane_base + P_COL;
-    const uint32_t t_o = tmem + lane_base + O_COL;
-    const long long row_limit = static_cast<long long>(q0) + r + p.past_len;  // last visible key
-    const long long tile_limit = static_cast<long long>(q0) + p.past_len;     // row 0's limit
-    const float sl2 = p.scale_log2;
-    float m_run = -INFINITY;  // running max of scaled scores, log2 units
-    float l_run = 0.f;        // running sum of exp2(x - m_run)
-    bool ok = true;
-
-    for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait(s, &s.s_full, j & 1)) { ok = false; break; }
-      tc_fence_after();
-      float x[BN];
-      {
-        uint32_t raw[BN / 32][32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_s + c * 32, raw[c]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          reg_fence(raw[c]);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(raw[c][i]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.s_free);
-
-      const long long kv0 = static_cast<long long>(j) * BN;
-      if (kv0 + BN - 1 > tile_limit) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (kv0 + c > row_limit) x[c] = -INFINITY;
-      }
-      float mx = x[0];
-#pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, x[c]);
-      const float m_new = fmaxf(m_run, mx * sl2);
-      bool need = false;
-      float factor = 1.f;
-      if (j == 0) {
-        m_run = m_new;
-      } else if (m_new > m_run + RESCALE_THRESHOLD) {
-        need = true;
-        factor = ex2_approx(m_run - m_new);
-        m_run = m_new;
-      }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      uint32_t pk[BN / 2];
-      float rowsum = 0.f;
-#pragma unroll
-      for (int c = 0; c < BN / 2; ++c) {
-        const float p0 = ex2_approx(fmaf(x[2 * c], sl2, -m_use));
-        const float p1 = ex2_approx(fmaf(x[2 * c + 1], sl2, -m_use));
-        rowsum += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
-      }
-      l_run = l_run * factor + rowsum;
-
-      if (j > 0) {
-        // P and O are still in use by P.V of the previous tile until pv_done flips.
-        if (!warp_wait(s, &s.pv_done, (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-          uint32_t o[HD / 32][32];
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            reg_fence(o[c]);
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * factor);
-            tmem_st32(t_o + c * 32, o[c]);
-          }
-        }
-      }
-      {
-        uint32_t half[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) half[i] = pk[i];
-        tmem_st32(t_p, half);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) half[i] = pk[32 + i];
-        tmem_st32(t_p + 32, half);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.p_ready);
-    }
-
-    if (ok && warp_wait(s, &s.pv_done, (n_kv - 1) & 1)) {
-      tc_fence_after();
-      const int row = q0 + r;
-      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint32_t o[HD / 32][32];
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
-      tmem_wait_ld();
-      if (row < p.Tq) {
-        __nv_bfloat16* orow =
-            p.o + (static_cast<size_t>(bh) * p.Tq + static_cast<size_t>(row)) * HD;
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          reg_fence(o[c]);
-          uint32_t packed[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            packed[i] = pack_bf16x2(__uint_as_float(o[c][2 * i]) * inv_l,
-                                    __uint_as_float(o[c][2 * i + 1]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                                packed[4 * i + 3]);
-        }
-        p.lse[static_cast<size_t>(bh) * p.Tq + row] =
-            l_run > 0.f ? (m_run + log2f(l_run)) * LN2 : -INFINITY;
-      }
-    }
+    regs_increase<SOFTMAX_REGS>();
+    const int t = warp / 4;
+    softmax_tile(s, p, tmem, t, warp % 4, lane, bh, q0[t], n_kv[t]);
   }
 
   tc_fence_before();

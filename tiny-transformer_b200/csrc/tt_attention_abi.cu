@@ -151,6 +151,20 @@ tt_attn_status prepare_device(int* dev_out) {
     return fail(TT_ATTN_UNSUPPORTED, buf);
   }
   if (!ds.attrs_set) {
+    // The prefill kernel hands registers between warpgroups (setmaxnreg); that is only
+    // sound when it launches with exactly the register count the hand-over was sized for.
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, tt::prefill::attention_prefill_kernel);
+    if (e != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncGetAttributes: ") + cudaGetErrorString(e));
+    if (fa.numRegs != static_cast<int>(tt::prefill::LAUNCH_REGS)) {
+      char buf[160];
+      std::snprintf(buf, sizeof(buf),
+                    "prefill kernel was compiled with %d registers per thread, expected %u; "
+                    "rebuild libtt_attention.so",
+                    fa.numRegs, tt::prefill::LAUNCH_REGS);
+      return fail(TT_ATTN_UNSUPPORTED, buf);
+    }
     e = cudaFuncSetAttribute(tt::prefill::attention_prefill_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(tt::prefill::kSmemBytes));
@@ -260,10 +274,10 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
       return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
     grid = bh * n_chunks;
   } else {
-    const int64_t n_qtiles = (q_len + tt::prefill::BM - 1) / tt::prefill::BM;
-    if (n_qtiles > INT32_MAX / bh)
+    const int64_t n_qblocks = (q_len + tt::prefill::BLOCK_M - 1) / tt::prefill::BLOCK_M;
+    if (n_qblocks > INT32_MAX / bh)
       return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
-    grid = bh * n_qtiles;
+    grid = bh * n_qblocks;
   }
 
   const Shape4 qs = canonical(batch, heads, q_len, q_strides);
@@ -328,7 +342,7 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
   p.Tq = static_cast<int>(q_len);
   p.Tk = static_cast<int>(kv_len);
   p.past_len = static_cast<int>(past_len);
-  p.n_qtiles = static_cast<int>((q_len + tt::prefill::BM - 1) / tt::prefill::BM);
+  p.n_qblocks = static_cast<int>((q_len + tt::prefill::BLOCK_M - 1) / tt::prefill::BLOCK_M);
   p.o = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
   p.scale_log2 = kScaleLog2;
