@@ -100,6 +100,27 @@ TT_ATTN_API const char* tt_attn_last_error(void);
 
 TT_ATTN_API int tt_attn_abi_version(void);
 
+/*
+ * Single-token decode that allocates nothing, not even through the caller. No counterpart in
+ * the reference: it exists for callers that cannot allocate device memory when they decode
+ * (a server whose memory is entirely reserved by its own pools, a Go/Java/Rust host calling
+ * this C ABI without a CUDA allocator, a loop that must stay out of the driver's allocator).
+ *
+ * Same computation and arguments as tt_attn_forward_bf16 with q_len = 1, head_dim = 64 and
+ * past_len = kv_len - 1; the split-KV partials live in a static device array of 8 MiB
+ * (8388608 bytes) that every GPU loading this library holds until exit. Shapes whose partials
+ * exceed it (tt_attn_forward_workspace_size) return TT_ATTN_BAD_ARG. The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. All calls share the array:
+ * calls whose kernels overlap on the GPU (different streams, or different host threads) race
+ * on it and must be serialised by the caller.
+ */
+TT_ATTN_API tt_attn_status tt_attn_decode_bf16_noalloc(
+    const void* q, const int64_t* q_strides,
+    const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides,
+    int64_t batch, int64_t heads, int64_t kv_len, const int32_t* kv_lens,
+    void* out, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -352,3 +352,64 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation decode
+// Some callers cannot allocate device memory at the moment they decode: an inference server
+// that reserved all of the GPU's memory for its own pools up front, a host language runtime
+// (Go, Java, Rust) driving this library over its C ABI without a CUDA allocator of its own,
+// or a latency-critical loop that must not enter the driver's allocator. For them the split-KV
+// partials live in this file-scope device array instead of a caller-provided workspace.
+// Every GPU that loads this library holds the array until the process exits.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB of decode partials
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Host code must not use the array's name as a device address: it is a host-side stand-in.
+// The device address is fetched once per device with that device current.
+void* g_noalloc_scratch_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" {
+
+TT_ATTN_API tt_attn_status tt_attn_decode_bf16_noalloc(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, int64_t batch, int64_t heads, int64_t kv_len,
+    const int32_t* kv_lens, void* out, float* lse, void* stream) {
+  if (batch <= 0 || heads <= 0 || kv_len <= 0)
+    return fail(TT_ATTN_BAD_ARG, "attention batch, heads and sequence lengths must be positive");
+  const size_t need = tt_attn_forward_workspace_size(batch, heads, 1, kv_len);
+  if (need > kNoAllocScratchBytes) {
+    char buf[200];
+    std::snprintf(buf, sizeof(buf),
+                  "decode of this shape needs %zu bytes of scratch; the no-allocation entry point "
+                  "holds at most %zu bytes: use tt_attn_forward_bf16 with a workspace",
+                  need, kNoAllocScratchBytes);
+    return fail(TT_ATTN_BAD_ARG, buf);
+  }
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TT_ATTN_UNSUPPORTED, "device index out of range");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      const cudaError_t se = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (se != cudaSuccess || ptr == nullptr)
+        return fail(TT_ATTN_LAUNCH_FAIL,
+                    std::string("cudaGetSymbolAddress(no-allocation scratch): ") +
+                        cudaGetErrorString(se));
+      g_noalloc_scratch_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  // The partials are written before they are read on every call, so nothing has to be cleared.
+  return tt_attn_forward_bf16(q, q_strides, k, k_strides, v, v_strides, batch, heads, 1, kv_len,
+                              TT_ATTN_HEAD_DIM, kv_len - 1, kv_lens, out, lse, scratch,
+                              kNoAllocScratchBytes, stream);
+}
+
+}  // extern "C"
