@@ -84,13 +84,13 @@ def test_unsupported_layouts(lib):
 
 def test_workspace_and_layout_queries(lib):
     # Decode with enough keys splits into several chunks and needs partials.
-    n = lib.tt_attn_forward_workspace_size(8, 12, 1, 512)
-    assert n > 0 and n % (66 * 4) == 0
-    assert lib.tt_attn_forward_workspace_size(8, 12, 1, 64) == 0   # one chunk per sequence
+    n = lib.tt_attn_forward_workspace_size(8, 12, 1, 4096)
+    assert n > 256 and (n - 256) % (68 * 4) == 0   # work counter + partials
+    assert lib.tt_attn_forward_workspace_size(8, 12, 1, 16) == 256  # one chunk: counter only
     assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # prefill needs none
     assert lib.tt_attn_forward_workspace_size(0, 12, 1, 512) == 0
     # Missing workspace for a split decode is rejected.
-    assert _call(lib, B=8, H=12, tq=1, tk=512, past=511) == 1
+    assert _call(lib, B=8, H=12, tq=1, tk=4096, past=4095) == 1
     assert "workspace" in _err(lib)
     assert lib.tt_attn_layout_supported(16, _strides(4096, 4096, 64, 1)) == 1
     assert lib.tt_attn_layout_supported(17, _strides(4096, 4096, 64, 1)) == 0

@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdio>
@@ -55,10 +56,14 @@ bool strides_ok(const int64_t* st) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Keys per decode CTA: the largest of 256/128/64 that still gives >= ~6 CTAs per SM.
+// Keys per decode work item: the largest power of two in [MIN_CHUNK, MAX_CHUNK] that still
+// gives about 8 items per CTA of a persistent grid on a 148-SM part, for load balance (a
+// shape-only heuristic, so the workspace size does not depend on the device).
 int decode_chunk(int64_t bh, int64_t tk) {
+  constexpr int64_t kTargetItems = 8 * 148;
   int chunk = tt::decode::MAX_CHUNK;
-  while (chunk > tt::decode::SUB && bh * ((tk + chunk - 1) / chunk) < 6 * 148) chunk /= 2;
+  while (chunk > tt::decode::MIN_CHUNK && bh * ((tk + chunk - 1) / chunk) < kTargetItems)
+    chunk /= 2;
   return chunk;
 }
 
@@ -115,11 +120,12 @@ struct DeviceState {
   bool checked = false;
   bool supported = false;
   bool attrs_set = false;
+  int sm_count = 0;
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
 
-tt_attn_status prepare_device(int* dev_out) {
+tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
@@ -134,6 +140,9 @@ tt_attn_status prepare_device(int* dev_out) {
     if (e != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
     ds.supported = (major == 10);
+    e = cudaDeviceGetAttribute(&ds.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
     ds.checked = true;
     if (!ds.supported) {
       char buf[160];
@@ -171,11 +180,12 @@ tt_attn_status prepare_device(int* dev_out) {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * tt::decode::MAX_CHUNK * tt::decode::ROW_BYTES);
+                               static_cast<int>(tt::decode::kSmemBytes));
     if (e != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     ds.attrs_set = true;
   }
+  if (sm_count) *sm_count = ds.sm_count;
   return TT_ATTN_OK;
 }
 
@@ -213,12 +223,16 @@ TT_ATTN_API int tt_attn_layout_supported(const void* ptr, const int64_t* strides
 TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, int64_t q_len,
                                                   int64_t kv_len) {
   if (batch <= 0 || heads <= 0 || q_len != 1 || kv_len <= 0 || kv_len > INT32_MAX) return 0;
+  if (batch > INT32_MAX / heads) return 0;
   const int64_t bh = batch * heads;
   const int chunk = decode_chunk(bh, kv_len);
   const int64_t n_chunks = (kv_len + chunk - 1) / chunk;
-  if (n_chunks <= 1) return 0;
-  return static_cast<size_t>(bh) * static_cast<size_t>(n_chunks) * tt::decode::PARTIAL *
-         sizeof(float);
+  // Decode: the work counter, then (with more than one chunk) the FP32 partials.
+  size_t bytes = tt::decode::kCounterBytes;
+  if (n_chunks > 1)
+    bytes += static_cast<size_t>(bh) * static_cast<size_t>(n_chunks) * tt::decode::PARTIAL *
+             sizeof(float);
+  return bytes;
 }
 
 TT_ATTN_API int tt_attn_device_supported(void) {
@@ -272,7 +286,7 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     n_chunks = (kv_len + chunk - 1) / chunk;
     if (n_chunks > INT32_MAX / bh)
       return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
-    grid = bh * n_chunks;
+    grid = bh * n_chunks;  // work items; the persistent grid is sized below
   } else {
     const int64_t n_qblocks = (q_len + tt::prefill::BLOCK_M - 1) / tt::prefill::BLOCK_M;
     if (n_qblocks > INT32_MAX / bh)
@@ -293,8 +307,8 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
   if (ws_needed > 0 && (workspace == nullptr || workspace_bytes < ws_needed))
     return fail(TT_ATTN_BAD_ARG, "workspace is smaller than tt_attn_forward_workspace_size()");
 
-  int dev = 0;
-  tt_attn_status st = prepare_device(&dev);
+  int dev = 0, sm_count = 0;
+  tt_attn_status st = prepare_device(&dev, &sm_count);
   if (st != TT_ATTN_OK) return st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
 
@@ -319,14 +333,38 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     p.n_chunks = static_cast<int>(n_chunks);
     p.o = static_cast<__nv_bfloat16*>(out);
     p.lse = lse;
-    p.partials = static_cast<float*>(workspace);
+    p.counter = static_cast<unsigned*>(workspace);
+    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                          tt::decode::kCounterBytes);
     p.scale_log2 = kScaleLog2;
-    const size_t smem = 2u * static_cast<size_t>(chunk) * tt::decode::ROW_BYTES;
-    tt::decode::decode_split_kernel<<<static_cast<unsigned>(grid), tt::decode::THREADS, smem, cs>>>(p);
+    // The CTAs take work items from a counter that must start at zero.
+    const cudaError_t me = cudaMemsetAsync(p.counter, 0, sizeof(unsigned), cs);
+    if (me != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaMemsetAsync(work counter): ") +
+                                           cudaGetErrorString(me));
+    // Persistent grid: one CTA per SM streams work items; no more CTAs than items.
+    const int64_t ctas = std::min<int64_t>(sm_count, grid);
+    tt::decode::decode_split_kernel<<<static_cast<unsigned>(ctas), tt::decode::THREADS,
+                                      tt::decode::kSmemBytes, cs>>>(p);
     if ((st = check_launch("decode_split_kernel launch")) != TT_ATTN_OK) return st;
     if (n_chunks > 1) {
-      tt::decode::decode_combine_kernel<<<static_cast<unsigned>(bh), tt::decode::HD, 0, cs>>>(p);
-      if ((st = check_launch("decode_combine_kernel launch")) != TT_ATTN_OK) return st;
+      // Programmatic dependent launch: the combine grid may start while the split grid drains;
+      // it waits (griddepcontrol.wait) for the split grid's memory before reading partials.
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(static_cast<unsigned>((bh + tt::decode::COMBINE_WARPS - 1) /
+                                               tt::decode::COMBINE_WARPS));
+      cfg.blockDim = dim3(tt::decode::COMBINE_WARPS * 32);
+      cfg.dynamicSmemBytes = 0;
+      cfg.stream = cs;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      const cudaError_t le = cudaLaunchKernelEx(&cfg, tt::decode::decode_combine_kernel, p);
+      if (le != cudaSuccess)
+        return fail(TT_ATTN_LAUNCH_FAIL, std::string("decode_combine_kernel launch: ") +
+                                             cudaGetErrorString(le));
     }
     return TT_ATTN_OK;
   }
