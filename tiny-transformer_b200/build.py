@@ -67,7 +67,9 @@ def _run(cmd: list[str], verbose: bool) -> str:
 
 # The prefill kernel re-allocates registers between warpgroups (setmaxnreg); its launch register
 # count must equal the value that hand-over was sized for (prefill_sm100.cuh: LAUNCH_REGS).
-PREFILL_LAUNCH_REGS = 168
+def _prefill_launch_regs() -> int:
+    text = open(os.path.join(CSRC, "prefill_sm100.cuh")).read()
+    return int(re.search(r"constexpr uint32_t LAUNCH_REGS = (\d+);", text).group(1))
 
 
 def _check_ptxas(report: str) -> None:
@@ -78,10 +80,11 @@ def _check_ptxas(report: str) -> None:
                 m = re.search(r"Used (\d+) registers", follow)
                 if m:
                     regs = int(m.group(1))
-                    if regs != PREFILL_LAUNCH_REGS:
+                    want = _prefill_launch_regs()
+                    if regs != want:
                         raise RuntimeError(
                             f"attention_prefill_kernel compiled with {regs} registers, expected "
-                            f"{PREFILL_LAUNCH_REGS}: the setmaxnreg hand-over would not be sound")
+                            f"{want}: the setmaxnreg hand-over would not be sound")
                     return
     raise RuntimeError("ptxas report for attention_prefill_kernel not found")
 
