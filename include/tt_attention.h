@@ -94,6 +94,13 @@ TT_ATTN_API int tt_attn_device_supported(void);
  * bit 0 = a bounded wait inside a kernel ran out. Synchronises the device. */
 TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear);
 
+/* Diagnostic for the failure path: launches one warp on `stream` that waits on a barrier
+ * phase nothing completes, bounded by `budget_cycles` (1 .. 1e9 SM clock cycles). The wait
+ * gives up by itself and sets bit 0 of the device status, which the caller then reads (and
+ * clears) with tt_attn_device_status; the context stays usable. No counterpart in the
+ * reference, which has no bounded waits. Returns BAD_ARG for a budget outside the range. */
+TT_ATTN_API tt_attn_status tt_attn_selftest_wait_timeout(int64_t budget_cycles, void* stream);
+
 /* Human-readable name of a status code. */
 TT_ATTN_API const char* tt_attn_status_string(tt_attn_status status);
 

@@ -64,13 +64,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 
 // Wait until the phase with the given parity has completed. Returns false (and
 // flags TT_ERR_TIMEOUT) if that takes longer than the cycle budget.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          long long budget = kWaitBudgetCycles) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
-    if (clock64() - t0 > kWaitBudgetCycles) {
+    if (clock64() - t0 > budget) {
       atomicOr(&g_tt_status, TT_ERR_TIMEOUT);
       return false;
     }

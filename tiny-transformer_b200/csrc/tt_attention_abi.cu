@@ -18,6 +18,7 @@
 #include "sm100_ptx.cuh"
 #include "prefill_sm100.cuh"
 #include "decode_sm100.cuh"
+#include "selftest_sm100.cuh"
 
 namespace {
 
@@ -253,6 +254,17 @@ TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear) {
   }
   if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("status read: ") + cudaGetErrorString(e));
   return (*flags & tt::TT_ERR_TIMEOUT) ? TT_ATTN_TIMEOUT : TT_ATTN_OK;
+}
+
+TT_ATTN_API tt_attn_status tt_attn_selftest_wait_timeout(int64_t budget_cycles, void* stream) {
+  if (budget_cycles < 1 || budget_cycles > tt::selftest::kMaxSelftestBudget)
+    return fail(TT_ATTN_BAD_ARG, "budget_cycles must be in [1, 1e9]");
+  int dev = 0;
+  tt_attn_status st = prepare_device(&dev);
+  if (st != TT_ATTN_OK) return st;
+  tt::selftest::wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<long long>(budget_cycles));
+  return check_launch("wait_timeout_kernel launch");
 }
 
 TT_ATTN_API tt_attn_status tt_attn_forward_bf16(

@@ -52,6 +52,8 @@ def load_c_abi() -> ctypes.CDLL:
     lib.tt_attn_device_supported.argtypes = []
     lib.tt_attn_device_status.restype = ctypes.c_int
     lib.tt_attn_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
+    lib.tt_attn_selftest_wait_timeout.restype = ctypes.c_int
+    lib.tt_attn_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
     lib.tt_attn_status_string.restype = ctypes.c_char_p
     lib.tt_attn_status_string.argtypes = [ctypes.c_int]
     lib.tt_attn_last_error.restype = ctypes.c_char_p
