@@ -7,7 +7,9 @@ B=4 H=12 Tq=Tk=4096 D=64 BF16 N(0,1), one step = one forward call; metric TFLOP/
 visible (i, j) pairs (4*B*H*D*T(T+1)/2 FLOP). The same line carries a ``decode`` block for
 BASELINE config 4 (B=64 H=12 Tk=8192 decode, per-sequence lengths U[1024, 8192] by seed),
 metric GB/s of the visible K/V rows plus q, O and LSE. ``--workload decode`` prints the decode
-measurement as the headline instead.
+measurement as the headline instead; ``--workload generation`` times BASELINE config 5 (greedy
+generation through a random-init decoder, TTFT / TPOT / tokens per second per attention
+backend).
 
 Multi-GPU (torchrun, one process per GPU): each rank owns an independent shard of the same shape
 (weak scaling: the (batch x head) work of prefill and the batch of decode partition without any
@@ -443,6 +445,59 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+GEN_CFG = {"batch": 32, "prompt": 128, "new_tokens": 256, "seed": 1234}
+
+
+def run_generation(args):
+    """greedy generation with a random-init decoder shaped like the
+    reference's configs/model_60m.json (8 layers, dim 768, 12 x 64 heads, SwiGLU 2048, vocab
+    8192, tied, BF16 N(0, 0.02) weights), batch 32, prompt 128 ids uniform in [0, 8192) by seed,
+    256 new tokens. Timed like the reference's model benchmark (benchmarks/model.py): host wall
+    time around device synchronisations, one warm-up request, medians over ``--steps`` requests.
+    Attention backends: student eager (the reference's call sequence, cache prefix views read in
+    place), student graphed (one CUDA graph per decode step over the full-capacity cache with
+    device-held kv_lens), torch SDPA and the reference specification. One GPU; under torchrun
+    only rank 0 runs."""
+    import statistics
+
+    import torch
+    import __graft_entry__
+    __graft_entry__.import_package()
+    from tiny_transformer_b200.generation import Decoder, DecoderConfig, request
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    torch.manual_seed(GEN_CFG["seed"])
+    model = Decoder(DecoderConfig(), "student").to(device="cuda", dtype=torch.bfloat16).eval()
+    g = torch.Generator(device="cuda").manual_seed(GEN_CFG["seed"])
+    prompt = torch.randint(0, model.config.vocab_size, (GEN_CFG["batch"], GEN_CFG["prompt"]),
+                           device="cuda", generator=g)
+    repeats = max(1, min(args.steps, 5))
+    results = {}
+    for name, backend, graphed in (("student_graphed", "student", True),
+                                   ("student", "student", False), ("sdpa", "sdpa", False),
+                                   ("reference", "reference", False)):
+        model.set_attention(backend)
+        request(model, prompt, GEN_CFG["new_tokens"], graphed=graphed)  # warm-up
+        trials = [request(model, prompt, GEN_CFG["new_tokens"], graphed=graphed)
+                  for _ in range(repeats)]
+        results[name] = {k: round(statistics.median(t[k] for t in trials), 4)
+                         for k in ("ttft_ms", "tpot_ms", "request_ms",
+                                   "output_tokens_per_second", "decode_tokens_per_second")}
+    head = results["student_graphed"]
+    line = {
+        "metric": "decode_tokens_per_second", "value": head["decode_tokens_per_second"],
+        "unit": "tokens/s", "n_gpus": 1, "steps": repeats, "warmup": 1,
+        "ms_per_step": head["request_ms"], "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic ids, random-init weights",
+        "config": {"workload": "cfg5 greedy generation, model_60m shape, batch 32, prompt 128, "
+                               "256 new tokens, attention=student (graphed decode)",
+                   "kv_capacity": GEN_CFG["prompt"] + GEN_CFG["new_tokens"]},
+        "backends": results,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_profile_case(which):
     """A few launches of one kernel at BASELINE size, for ncu captures (no timing, no CPU leg):
     two warm-up calls then one profiled call."""
@@ -470,7 +525,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("prefill", "decode"), default="prefill")
+    ap.add_argument("--workload", choices=("prefill", "decode", "generation"), default="prefill")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--profile", choices=("prefill", "decode"), default=None,
                     help="run 3 launches of one kernel for an ncu capture and exit")
@@ -479,7 +534,9 @@ def main():
     if args.profile:
         run_profile_case(args.profile)
         return
-    if args.impl == "reference":
+    if args.workload == "generation":
+        run_generation(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
