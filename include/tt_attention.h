@@ -91,8 +91,35 @@ TT_ATTN_API int tt_attn_layout_supported(const void* ptr, const int64_t* strides
 TT_ATTN_API int tt_attn_device_supported(void);
 
 /* Reads (and, when clear != 0, resets) the current device's kernel status bits:
- * bit 0 = a bounded wait inside a kernel ran out. Synchronises the device. */
+ * bit 0 = a bounded wait inside a kernel ran out (returns TT_ATTN_TIMEOUT);
+ * bit 1 = tt_rope_append_bf16 met a device-held position outside the cache or the table and
+ * skipped those rows (returns TT_ATTN_BAD_ARG). Synchronises the device. */
 TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear);
+
+/*
+ * Fused rotary embedding + KV-cache append for one decoder layer (the step before attention
+ * in Block.forward, tiny_transformer/model.py:61-68: reference.rope on q and k, reference.py:
+ * 30-34, then KVCache.update, model.py:29-41). Replaces for this path the reference's
+ * `rope` operator calls (student rope_forward) plus the two cache copies.
+ *
+ *   qkv      [batch, q_len, 3, heads, 64] bf16, contiguous (the fused QKV projection)
+ *   cos, sin [table_len, 32] FP32 contiguous, row = position (rounded to bf16 as the
+ *            reference's cos.to(x.dtype) does)
+ *   q_out    [batch, heads, q_len, 64] bf16 contiguous: rope(q)
+ *   cache_k / cache_v [batch, heads, capacity, 64] bf16, last stride 1, element strides in
+ *            ck_strides / cv_strides (4 entries); row `position + t` receives rope(k) / v.
+ *
+ * The start position is `position` or, when `position_dev` is not NULL, the int64 it points
+ * to on the device (read at run time, so a captured CUDA graph can serve every step). Host
+ * positions are validated here (BAD_ARG); device-held ones by the kernel, which skips rows
+ * outside [0, min(capacity, table_len)) and sets status bit 1. Bit-exact with the reference's
+ * bf16 expression. All pointers 4-byte aligned; 16-byte aligned rows are fastest.
+ */
+TT_ATTN_API tt_attn_status tt_rope_append_bf16(
+    const void* qkv, int64_t batch, int64_t q_len, int64_t heads, const float* cos,
+    const float* sin, int64_t table_len, int64_t position, const int64_t* position_dev,
+    void* q_out, void* cache_k, const int64_t* ck_strides, void* cache_v,
+    const int64_t* cv_strides, int64_t capacity, void* stream);
 
 /* Diagnostic for the failure path: launches one warp on `stream` that waits on a barrier
  * phase nothing completes, bounded by `budget_cycles` (1 .. 1e9 SM clock cycles). The wait

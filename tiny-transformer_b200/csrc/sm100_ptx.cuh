@@ -16,6 +16,7 @@ namespace tt {
 // host reads and clears it through tt_attn_device_status() (tt_attention_abi.cu).
 enum : unsigned {
   TT_ERR_TIMEOUT = 1u,  // an mbarrier wait exceeded kWaitBudgetCycles
+  TT_ERR_RANGE = 2u,    // a device-held position was outside its buffer; the write was skipped
 };
 static __device__ unsigned g_tt_status = 0;
 

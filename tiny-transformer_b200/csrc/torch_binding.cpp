@@ -139,12 +139,67 @@ std::tuple<torch::Tensor, torch::Tensor> attention_forward(
   return {o, lse};
 }
 
+// Fused RoPE + KV-cache append (tt_rope_append_bf16). `position` is either a Python int or an
+// int64 CUDA tensor with one element (read on the device, for captured decode steps).
+torch::Tensor rope_append(const torch::Tensor& qkv, const torch::Tensor& cos,
+                          const torch::Tensor& sin, const pybind11::object& position,
+                          torch::Tensor cache_k, torch::Tensor cache_v) {
+  TORCH_CHECK(qkv.is_cuda() && cos.is_cuda() && sin.is_cuda() && cache_k.is_cuda() &&
+                  cache_v.is_cuda(), "rope_append: all tensors must be CUDA tensors");
+  for (const torch::Tensor* t : {&cos, &sin, static_cast<const torch::Tensor*>(&cache_k),
+                                 static_cast<const torch::Tensor*>(&cache_v)})
+    TORCH_CHECK(t->device() == qkv.device(), "rope_append: all tensors must be on the same device");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && cache_k.scalar_type() == at::kBFloat16 &&
+                  cache_v.scalar_type() == at::kBFloat16, "rope_append: qkv and caches must be bf16");
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat,
+              "rope_append: cos/sin tables must be float32");
+  TORCH_CHECK(qkv.dim() == 5 && qkv.size(2) == 3 && qkv.size(4) == TT_ATTN_HEAD_DIM &&
+                  qkv.is_contiguous(), "rope_append: qkv must be a contiguous [B, T, 3, H, 64] tensor");
+  TORCH_CHECK(cos.dim() == 2 && cos.size(1) == TT_ATTN_HEAD_DIM / 2 && cos.is_contiguous() &&
+                  sin.sizes() == cos.sizes() && sin.is_contiguous(),
+              "rope_append: cos/sin must be contiguous [L, 32] tables");
+  const int64_t B = qkv.size(0), T = qkv.size(1), H = qkv.size(3);
+  for (const torch::Tensor* c : {&cache_k, &cache_v})
+    TORCH_CHECK(c->dim() == 4 && c->size(0) == B && c->size(1) == H &&
+                    c->size(3) == TT_ATTN_HEAD_DIM && c->stride(3) == 1,
+                "rope_append: caches must be [B, H, capacity, 64] with contiguous rows");
+  TORCH_CHECK(cache_v.size(2) == cache_k.size(2), "rope_append: caches must have equal capacity");
+  int64_t pos = 0;
+  const int64_t* pos_dev = nullptr;
+  torch::Tensor pos_t;
+  if (pybind11::isinstance<pybind11::int_>(position)) {
+    pos = position.cast<int64_t>();
+  } else {
+    pos_t = position.cast<torch::Tensor>();
+    TORCH_CHECK(pos_t.is_cuda() && pos_t.device() == qkv.device() &&
+                    pos_t.scalar_type() == at::kLong && pos_t.numel() == 1,
+                "rope_append: a tensor position must be a one-element int64 CUDA tensor");
+    pos_dev = pos_t.data_ptr<int64_t>();
+  }
+  const c10::cuda::CUDAGuard device_guard(qkv.device());
+  auto q_out = torch::empty({B, H, T, TT_ATTN_HEAD_DIM}, qkv.options());
+  const int64_t ks[4] = {cache_k.stride(0), cache_k.stride(1), cache_k.stride(2), 1};
+  const int64_t vs[4] = {cache_v.stride(0), cache_v.stride(1), cache_v.stride(2), 1};
+  auto stream = c10::cuda::getCurrentCUDAStream(qkv.get_device());
+  const tt_attn_status st = tt_rope_append_bf16(
+      qkv.data_ptr(), B, T, H, cos.data_ptr<float>(), sin.data_ptr<float>(), cos.size(0), pos,
+      pos_dev, q_out.data_ptr(), cache_k.data_ptr(), ks, cache_v.data_ptr(), vs, cache_k.size(2),
+      static_cast<void*>(stream.stream()));
+  TORCH_CHECK(st == TT_ATTN_OK, "tt_rope_append_bf16 failed: ", tt_attn_status_string(st), ": ",
+              tt_attn_last_error());
+  return q_out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_forward", &attention_forward,
         "BF16 causal attention forward on sm_100a (returns O and natural-log FP32 LSE)",
         pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"),
         pybind11::arg("past_len") = 0, pybind11::arg("segment_ids") = pybind11::none(),
         pybind11::arg("kv_lens") = pybind11::none());
+  m.def("rope_append", &rope_append,
+        "Fused RoPE on q/k of a [B, T, 3, H, 64] QKV projection + KV-cache append; returns rope(q)",
+        pybind11::arg("qkv"), pybind11::arg("cos"), pybind11::arg("sin"),
+        pybind11::arg("position"), pybind11::arg("cache_k"), pybind11::arg("cache_v"));
   m.attr("HEAD_DIM") = TT_ATTN_HEAD_DIM;
   m.attr("ABI_VERSION") = TT_ATTN_ABI_VERSION;
 }

@@ -19,6 +19,7 @@
 #include "prefill_sm100.cuh"
 #include "decode_sm100.cuh"
 #include "selftest_sm100.cuh"
+#include "rope_append_sm100.cuh"
 
 namespace {
 
@@ -253,7 +254,61 @@ TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear) {
     e = cudaMemcpyToSymbol(tt::g_tt_status, &zero, sizeof(unsigned));
   }
   if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("status read: ") + cudaGetErrorString(e));
-  return (*flags & tt::TT_ERR_TIMEOUT) ? TT_ATTN_TIMEOUT : TT_ATTN_OK;
+  if (*flags & tt::TT_ERR_TIMEOUT) return TT_ATTN_TIMEOUT;
+  return (*flags & tt::TT_ERR_RANGE) ? TT_ATTN_BAD_ARG : TT_ATTN_OK;
+}
+
+TT_ATTN_API tt_attn_status tt_rope_append_bf16(
+    const void* qkv, int64_t batch, int64_t q_len, int64_t heads, const float* cos,
+    const float* sin, int64_t table_len, int64_t position, const int64_t* position_dev,
+    void* q_out, void* cache_k, const int64_t* ck_strides, void* cache_v,
+    const int64_t* cv_strides, int64_t capacity, void* stream) {
+  if (!qkv || !cos || !sin || !q_out || !cache_k || !cache_v || !ck_strides || !cv_strides)
+    return fail(TT_ATTN_BAD_ARG, "rope_append: pointers must not be NULL");
+  if (batch <= 0 || q_len <= 0 || heads <= 0 || capacity <= 0 || table_len <= 0)
+    return fail(TT_ATTN_BAD_ARG, "rope_append: sizes must be positive");
+  if (ck_strides[3] != 1 || cv_strides[3] != 1)
+    return fail(TT_ATTN_BAD_ARG, "rope_append: cache rows must be contiguous (last stride 1)");
+  for (int i = 0; i < 3; ++i)
+    if (ck_strides[i] % 2 != 0 || cv_strides[i] % 2 != 0)
+      return fail(TT_ATTN_BAD_ARG, "rope_append: cache strides must be even (4-byte pairs)");
+  for (const void* ptr : {qkv, static_cast<const void*>(q_out), static_cast<const void*>(cache_k),
+                          static_cast<const void*>(cache_v), static_cast<const void*>(cos),
+                          static_cast<const void*>(sin)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 4 != 0)
+      return fail(TT_ATTN_BAD_ARG, "rope_append: pointers must be 4-byte aligned");
+  const int64_t max_rows = static_cast<int64_t>(INT32_MAX) * tt::rope::ROWS_PER_BLOCK;
+  if (batch > INT32_MAX || q_len > INT32_MAX || heads > INT32_MAX ||
+      q_len > max_rows / heads / batch)
+    return fail(TT_ATTN_BAD_ARG, "rope_append: shape exceeds the supported grid");
+  const int64_t rows = batch * q_len * heads;
+  if (position_dev == nullptr &&
+      (position < 0 || position + q_len > capacity || position + q_len > table_len))
+    return fail(TT_ATTN_BAD_ARG, "rope_append: position + q_len exceeds the cache capacity or "
+                                 "the cos/sin table");
+  int dev = 0;
+  tt_attn_status st = prepare_device(&dev);
+  if (st != TT_ATTN_OK) return st;
+  tt::rope::Params p{};
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.B = static_cast<int>(batch);
+  p.T = static_cast<int>(q_len);
+  p.H = static_cast<int>(heads);
+  p.cos = cos;
+  p.sin = sin;
+  p.table_len = table_len;
+  p.position = position;
+  p.position_dev = reinterpret_cast<const long long*>(position_dev);
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.cache_k = static_cast<__nv_bfloat16*>(cache_k);
+  p.cache_v = static_cast<__nv_bfloat16*>(cache_v);
+  p.ck_s0 = ck_strides[0]; p.ck_s1 = ck_strides[1]; p.ck_s2 = ck_strides[2];
+  p.cv_s0 = cv_strides[0]; p.cv_s1 = cv_strides[1]; p.cv_s2 = cv_strides[2];
+  p.capacity = capacity;
+  const unsigned grid =
+      static_cast<unsigned>((rows + tt::rope::ROWS_PER_BLOCK - 1) / tt::rope::ROWS_PER_BLOCK);
+  tt::rope::rope_append_kernel<<<grid, tt::rope::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("rope_append_kernel launch");
 }
 
 TT_ATTN_API tt_attn_status tt_attn_selftest_wait_timeout(int64_t budget_cycles, void* stream) {

@@ -14,7 +14,11 @@ Two decode paths:
   them in place (row stride = 128 B), where the reference's native path copies the whole
   prefix of every layer at every step (attention.cu:74-76).
 * graphed (``GraphedDecode``): one decode step (embedding, all layers, K/V append, attention,
-  logits, argmax, position advance) captured once in a CUDA graph. Attention reads the
+  logits, argmax, position advance) captured once in a CUDA graph.
+
+With the student attention and a cache, RoPE on q/k and the K/V append run as one kernel per
+layer (``operators.fused.rope_append``) reading FP32 cos/sin tables built once per model, in
+place of the reference's ~20 elementwise launches for ``rope`` and ``KVCache.update``. Attention reads the
   full-capacity cache with per-sequence lengths ``kv_lens`` held on the device, so the same
   graph serves every step and the host only replays it.
 
@@ -143,6 +147,14 @@ class KVCache:
         values[:, :, self.length:end, :].copy_(v)
         return keys[:, :, :end, :], values[:, :, :end, :]
 
+    def storage_for(self, layer, qkv):
+        """The layer's [B, H, capacity, D] storage for a [B, T, 3, H, D] projection."""
+        b, _, _, h, d = qkv.shape
+        if b != self.batch_size:
+            raise ValueError("KV cache capacity exceeded or batch size changed")
+        proto = qkv.new_empty((b, h, 1, d))
+        return self._storage(layer, proto, proto)
+
     def append_at(self, layer, k, v, position: torch.Tensor):
         """Write one step's keys/values at the device-held ``position`` (int64, shape [1]);
         returns the full-capacity storage. Used inside a captured decode step."""
@@ -193,6 +205,29 @@ class Block(nn.Module):
             k, v = cache.update(layer, k, v)
         return self.finish(x, attention(q, k, v, past_len))
 
+    def qkv_rows(self, x):
+        """The fused QKV projection as a contiguous [B, T, 3, H, 64] tensor."""
+        cfg = self.config
+        batch, time, _ = x.shape
+        h = rms_norm(x, self.attn_norm, cfg.norm_eps)
+        return F.linear(h, self.qkv).view(batch, time, 3, cfg.n_heads, cfg.head_dim)
+
+    def forward_fused(self, x, tables, layer, cache, position, kv_lens=None):
+        """Student path: one kernel applies RoPE to q/k and appends k/v to the cache
+        (operators.fused.rope_append), then attention reads the cache in place. With
+        ``kv_lens`` (captured decode) attention sees the full-capacity cache masked per
+        sequence; otherwise the live prefix [0, position + T)."""
+        from .operators import fused, student
+        qkv = self.qkv_rows(x)
+        keys, values = cache.storage_for(layer, qkv)
+        q = fused.rope_append(qkv, tables[0], tables[1], position, keys, values)
+        if kv_lens is not None:
+            attended = student.attention(q, keys, values, cache.capacity - 1, None, kv_lens)
+        else:
+            end = position + x.shape[1]
+            attended = student.attention(q, keys[:, :, :end], values[:, :, :end], position)
+        return self.finish(x, attended)
+
 
 class Decoder(nn.Module):
     """Decoder with tied embeddings (model.py:79-136), attention chosen by name."""
@@ -211,10 +246,33 @@ class Decoder(nn.Module):
         for block in self.blocks:
             for parameter in (block.proj, block.down):
                 nn.init.normal_(parameter, std=0.02 / (2 * config.n_layers) ** 0.5)
+        # RoPE tables for every position, FP32: the values model.py:114-118 computes per call,
+        # computed on the model's device like there (rebuilt whenever the model moves).
+        self.register_buffer("rope_cos", torch.empty(0), persistent=False)
+        self.register_buffer("rope_sin", torch.empty(0), persistent=False)
+        self._build_rope_tables()
+        # With the student attention, RoPE + cache append run as one fused kernel.
+        self.fused_rope = True
+
+    def _build_rope_tables(self):
+        positions = torch.arange(self.config.max_seq_len, device=self.embedding.device)
+        cos, sin = self.rope_tables(positions)
+        self.rope_cos = cos[0, 0].contiguous()
+        self.rope_sin = sin[0, 0].contiguous()
+
+    def _apply(self, fn, recurse=True):
+        # Moving or casting the model (e.g. .to("cuda", torch.bfloat16)) rebuilds the FP32
+        # tables on the new device instead of rounding or copying them.
+        out = super()._apply(fn, recurse)
+        self._build_rope_tables()
+        return out
 
     def set_attention(self, name: str):
         self.attention_name = name
         self.attention = attention_operator(name)
+
+    def uses_fused(self, cache) -> bool:
+        return cache is not None and self.fused_rope and self.attention_name == "student"
 
     def new_cache(self, batch_size, capacity=None):
         return KVCache(self.config, batch_size,
@@ -244,10 +302,15 @@ class Decoder(nn.Module):
                 raise ValueError("KV cache requires eval() and torch.no_grad()/inference_mode()")
             if time_ + past_len > cache.capacity or ids.shape[0] != cache.batch_size:
                 raise ValueError("KV cache capacity exceeded or batch size changed")
-        cos, sin = self.rope_tables(torch.arange(past_len, past_len + time_, device=ids.device))
         x = F.embedding(ids, self.embedding)
-        for layer, block in enumerate(self.blocks):
-            x = block(x, self.attention, cos, sin, layer, cache)
+        if self.uses_fused(cache):
+            tables = (self.rope_cos, self.rope_sin)
+            for layer, block in enumerate(self.blocks):
+                x = block.forward_fused(x, tables, layer, cache, past_len)
+        else:
+            cos, sin = self.rope_tables(torch.arange(past_len, past_len + time_, device=ids.device))
+            for layer, block in enumerate(self.blocks):
+                x = block(x, self.attention, cos, sin, layer, cache)
         if cache is not None:
             cache.length += time_
         if last_only:
@@ -301,14 +364,19 @@ class GraphedDecode:
         from .operators import student
         model, cache = self.model, self.cache
         cap = cache.capacity
-        cos, sin = model.rope_tables(self.position)
         x = F.embedding(self.token, model.embedding)
         self.kv_lens.copy_((self.position + 1).to(torch.int32).expand_as(self.kv_lens))
-        for layer, block in enumerate(model.blocks):
-            q, k, v = block.project_qkv(x, cos, sin)
-            keys, values = cache.append_at(layer, k, v, self.position)
-            attended = student.attention(q, keys, values, cap - 1, None, self.kv_lens)
-            x = block.finish(x, attended)
+        if model.fused_rope:
+            tables = (model.rope_cos, model.rope_sin)
+            for layer, block in enumerate(model.blocks):
+                x = block.forward_fused(x, tables, layer, cache, self.position, self.kv_lens)
+        else:
+            cos, sin = model.rope_tables(self.position)
+            for layer, block in enumerate(model.blocks):
+                q, k, v = block.project_qkv(x, cos, sin)
+                keys, values = cache.append_at(layer, k, v, self.position)
+                attended = student.attention(q, keys, values, cap - 1, None, self.kv_lens)
+                x = block.finish(x, attended)
         nxt = model.logits(x)[:, -1, :].argmax(dim=-1, keepdim=True)
         self.token.copy_(nxt)
         self.out.index_copy_(1, self.out_index, nxt)
