@@ -89,9 +89,10 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// 4-D map over [B, H, T, 64] bf16 (dims listed innermost first), box 64 x 128 rows,
+// 4-D map over [B, H, T, 64] bf16 (dims listed innermost first), box 64 x box_rows rows,
 // 128-byte swizzle; rows past T read as zero.
-bool encode_map(CUtensorMap* map, const void* base, const Shape4& s, std::string* err) {
+bool encode_map(CUtensorMap* map, const void* base, const Shape4& s, std::string* err,
+                unsigned box_rows = tt::prefill::BM) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) {
     *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
@@ -102,7 +103,7 @@ bool encode_map(CUtensorMap* map, const void* base, const Shape4& s, std::string
   const cuuint64_t strides[3] = {static_cast<cuuint64_t>(s.stride[2]) * 2,
                                  static_cast<cuuint64_t>(s.stride[1]) * 2,
                                  static_cast<cuuint64_t>(s.stride[0]) * 2};
-  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tt::prefill::BM), 1, 1};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -164,21 +165,23 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
   if (!ds.attrs_set) {
     // The prefill kernel hands registers between warpgroups (setmaxnreg); that is only
     // sound when it launches with exactly the register count the hand-over was sized for.
+    const void* prefill_fn = reinterpret_cast<const void*>(tt::prefill::attention_prefill_kernel);
+    const unsigned launch_regs = tt::prefill::LAUNCH_REGS;
+    const int prefill_smem = static_cast<int>(tt::prefill::kSmemBytes);
     cudaFuncAttributes fa{};
-    e = cudaFuncGetAttributes(&fa, tt::prefill::attention_prefill_kernel);
+    e = cudaFuncGetAttributes(&fa, prefill_fn);
     if (e != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncGetAttributes: ") + cudaGetErrorString(e));
-    if (fa.numRegs != static_cast<int>(tt::prefill::LAUNCH_REGS)) {
+    if (fa.numRegs != static_cast<int>(launch_regs)) {
       char buf[160];
       std::snprintf(buf, sizeof(buf),
                     "prefill kernel was compiled with %d registers per thread, expected %u; "
                     "rebuild libtt_attention.so",
-                    fa.numRegs, tt::prefill::LAUNCH_REGS);
+                    fa.numRegs, launch_regs);
       return fail(TT_ATTN_UNSUPPORTED, buf);
     }
-    e = cudaFuncSetAttribute(tt::prefill::attention_prefill_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(tt::prefill::kSmemBytes));
+    e = cudaFuncSetAttribute(prefill_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             prefill_smem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -438,8 +441,9 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
 
   CUtensorMap tmq, tmk, tmv;
   std::string err;
-  if (!encode_map(&tmq, q, qs, &err) || !encode_map(&tmk, k, ks, &err) ||
-      !encode_map(&tmv, v, vs, &err))
+  constexpr unsigned kv_box = tt::prefill::BN;
+  if (!encode_map(&tmq, q, qs, &err) || !encode_map(&tmk, k, ks, &err, kv_box) ||
+      !encode_map(&tmv, v, vs, &err, kv_box))
     return fail(TT_ATTN_UNSUPPORTED, err);
   tt::prefill::Params p{};
   p.B = static_cast<int>(batch);
