@@ -97,6 +97,39 @@ TT_ATTN_API int tt_attn_device_supported(void);
 TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear);
 
 /*
+ * BF16 causal attention backward: dQ, dK, dV from the forward's inputs, output O and LSE.
+ *
+ * Replaces `attention_backward(q, k, v, dO, O, lse, past_len, segment_ids)`
+ * (csrc/attention/attention.cu:161-234, declared in csrc/attention/attention.h, bound in
+ * csrc/attention/bindings.cpp), i.e. the preprocess, dKdV and dQ kernels
+ * (attention_backward_preprocess_kernel.cuh, attention_backward_dKdV_kernel.cu,
+ * attention_backward_dQ_kernel.cu). Same arithmetic: D = rowsum(dO * O), P = exp(S / 8 - LSE),
+ * dS = P * (dO.V^T - D), P and dS rounded to bf16 before the products, FP32 accumulation,
+ * dQ = dS.K / 8, dK = dS^T.Q / 8, dV = P^T.dO.
+ *
+ *   q, k, v     [batch, heads, q_len | kv_len, 64] bf16 with element strides (same layout rules
+ *               as tt_attn_forward_bf16; TT_ATTN_UNSUPPORTED otherwise)
+ *   dout, out   contiguous [batch, heads, q_len, 64] bf16 (dO and the forward's O)
+ *   lse         contiguous [batch, heads, q_len] FP32, natural log (the forward's LSE)
+ *   dq          contiguous [batch, heads, q_len, 64] bf16 output
+ *   dk, dv      contiguous [batch, heads, kv_len, 64] bf16 outputs
+ *   workspace   tt_attn_backward_workspace_size() bytes (the FP32 row sums D)
+ *
+ * Mask: key j visible to query i iff j <= i + past_len, kv_len == q_len + past_len.
+ * Three kernels are launched on `stream`, in order; nothing is allocated.
+ */
+TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, const void* dout, const void* out, const float* lse,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
+    int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+    void* stream);
+
+/* Bytes of workspace tt_attn_backward_bf16 needs (batch * heads * q_len FP32), 0 for invalid
+ * sizes. */
+TT_ATTN_API size_t tt_attn_backward_workspace_size(int64_t batch, int64_t heads, int64_t q_len);
+
+/*
  * Fused rotary embedding + KV-cache append for one decoder layer (the step before attention
  * in Block.forward, tiny_transformer/model.py:61-68: reference.rope on q and k, reference.py:
  * 30-34, then KVCache.update, model.py:29-41). Replaces for this path the reference's

@@ -83,8 +83,8 @@ std::tuple<torch::Tensor, torch::Tensor> attention_forward(
   check_mask(q, k, v, past_len);
   TORCH_CHECK(!(at::GradMode::is_enabled() &&
                 (q.requires_grad() || k.requires_grad() || v.requires_grad())),
-              "the sm_100a attention forward has no backward; "
-              "call it under torch.no_grad() or use inference tensors");
+              "student attention backward requires the Python autograd binding; "
+              "use student.attention or no_grad for inference");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16,
               "float32 attention is not provided by the sm_100a path; pass bf16 q, k, v");
   TORCH_CHECK(!segment_ids.has_value(), "segment_ids is not supported for bf16 kernel");
@@ -137,6 +137,79 @@ std::tuple<torch::Tensor, torch::Tensor> attention_forward(
   TORCH_CHECK(st == TT_ATTN_OK, "tt_attn_forward_bf16 failed: ", tt_attn_status_string(st),
               ": ", tt_attn_last_error());
   return {o, lse};
+}
+
+void check_upstream(const torch::Tensor& q, const torch::Tensor& dO, const torch::Tensor& o,
+                    const torch::Tensor& lse) {
+  for (const torch::Tensor* x : {&dO, &o, &lse}) {
+    TORCH_CHECK(x->defined(), "dO, O and LSE must be defined");
+    TORCH_CHECK(x->is_cuda() && x->device() == q.device(),
+                "dO, O and LSE must be CUDA tensors on the same device as q");
+    TORCH_CHECK(x->layout() == at::kStrided, "dO, O and LSE must have strided layout");
+  }
+  TORCH_CHECK(dO.scalar_type() == q.scalar_type() && o.scalar_type() == q.scalar_type(),
+              "dO and O must have the same dtype as q");
+  TORCH_CHECK(dO.sizes() == q.sizes() && o.sizes() == q.sizes(),
+              "dO and O must have the same shape as q");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat, "LSE must be float32");
+  TORCH_CHECK(lse.dim() == 3 && lse.size(0) == q.size(0) && lse.size(1) == q.size(1) &&
+                  lse.size(2) == q.size(2),
+              "LSE must have shape [B, Nh, Tq]");
+}
+
+// Contiguous, 16-byte aligned copy of x unless it already is one.
+torch::Tensor contiguous_aligned(torch::Tensor x) {
+  x = x.contiguous();
+  if (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 != 0) x = x.clone();
+  return x;
+}
+
+// The reference's native backward (attention.cu:161-234): same argument order, validation
+// order and message fragments; all device work through tt_attn_backward_bf16.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> attention_backward(
+    torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor dO, torch::Tensor O,
+    torch::Tensor lse, int64_t past_len, std::optional<torch::Tensor> segment_ids) {
+  check_tensors(q, k, v);
+  check_mask(q, k, v, past_len);
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16, "student attention backward supports only bf16");
+  TORCH_CHECK(!segment_ids.has_value(),
+              "segment_ids is not supported for bf16 attention backward");
+  check_upstream(q, dO, O, lse);
+  const int64_t B = q.size(0), H = q.size(1), Tq = q.size(2), Tk = k.size(2);
+  TORCH_CHECK(Tk <= std::numeric_limits<int32_t>::max(),
+              "bf16 attention sequence lengths must fit int32 (Tk <= INT32_MAX)");
+  const int64_t max_grid = std::numeric_limits<int32_t>::max();
+  const int64_t k_tiles = (Tk + 127) / 128;  // >= query tiles
+  TORCH_CHECK(B <= max_grid / H && k_tiles <= max_grid / (B * H),
+              "attention backward shape exceeds the supported CUDA grid limits");
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  const auto* props = at::cuda::getDeviceProperties(q.get_device());
+  TORCH_CHECK(props->major == 10,
+              "the bf16 attention kernels require an sm_100 GPU (compute capability 10.x); "
+              "found SM", props->major, props->minor);
+  auto stream = c10::cuda::getCurrentCUDAStream(q.get_device());
+  // Validated; now materialise the layouts the kernels read (on the current stream).
+  q = aligned_contiguous(q);
+  k = aligned_contiguous(k);
+  v = aligned_contiguous(v);
+  dO = contiguous_aligned(dO);
+  O = contiguous_aligned(O);
+  lse = lse.contiguous();
+  auto dq = torch::empty({B, H, Tq, TT_ATTN_HEAD_DIM}, q.options());
+  auto dk = torch::empty({B, H, Tk, TT_ATTN_HEAD_DIM}, q.options());
+  auto dv = torch::empty({B, H, Tk, TT_ATTN_HEAD_DIM}, q.options());
+  const size_t ws_bytes = tt_attn_backward_workspace_size(B, H, Tq);
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
+  const int64_t qs[4] = {q.stride(0), q.stride(1), q.stride(2), q.stride(3)};
+  const int64_t ks[4] = {k.stride(0), k.stride(1), k.stride(2), k.stride(3)};
+  const int64_t vs[4] = {v.stride(0), v.stride(1), v.stride(2), v.stride(3)};
+  const tt_attn_status st = tt_attn_backward_bf16(
+      q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, dO.data_ptr(), O.data_ptr(),
+      lse.data_ptr<float>(), B, H, Tq, Tk, TT_ATTN_HEAD_DIM, past_len, dq.data_ptr(),
+      dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes, static_cast<void*>(stream.stream()));
+  TORCH_CHECK(st == TT_ATTN_OK, "tt_attn_backward_bf16 failed: ", tt_attn_status_string(st),
+              ": ", tt_attn_last_error());
+  return {dq, dk, dv};
 }
 
 // Fused RoPE + KV-cache append (tt_rope_append_bf16). `position` is either a Python int or an
@@ -196,6 +269,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"),
         pybind11::arg("past_len") = 0, pybind11::arg("segment_ids") = pybind11::none(),
         pybind11::arg("kv_lens") = pybind11::none());
+  m.def("attention_backward", &attention_backward,
+        "BF16 causal attention backward on sm_100a (preprocess, dQ, dK/dV); returns dq, dk, dv",
+        pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("dO"),
+        pybind11::arg("O"), pybind11::arg("lse"), pybind11::arg("past_len") = 0,
+        pybind11::arg("segment_ids") = pybind11::none());
   m.def("rope_append", &rope_append,
         "Fused RoPE on q/k of a [B, T, 3, H, 64] QKV projection + KV-cache append; returns rope(q)",
         pybind11::arg("qkv"), pybind11::arg("cos"), pybind11::arg("sin"),

@@ -20,6 +20,7 @@
 #include "decode_sm100.cuh"
 #include "selftest_sm100.cuh"
 #include "rope_append_sm100.cuh"
+#include "backward_sm100.cuh"
 
 namespace {
 
@@ -186,6 +187,14 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tt::decode::kSmemBytes));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tt::backward::bwd_dq_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tt::backward::kSmemQ));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tt::backward::bwd_dkdv_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tt::backward::kSmemKV));
     if (e != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     ds.attrs_set = true;
@@ -312,6 +321,103 @@ TT_ATTN_API tt_attn_status tt_rope_append_bf16(
       static_cast<unsigned>((rows + tt::rope::ROWS_PER_BLOCK - 1) / tt::rope::ROWS_PER_BLOCK);
   tt::rope::rope_append_kernel<<<grid, tt::rope::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("rope_append_kernel launch");
+}
+
+TT_ATTN_API size_t tt_attn_backward_workspace_size(int64_t batch, int64_t heads, int64_t q_len) {
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || batch > INT32_MAX / heads || q_len > INT32_MAX)
+    return 0;
+  return static_cast<size_t>(batch * heads) * static_cast<size_t>(q_len) * sizeof(float);
+}
+
+TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, const void* dout, const void* out, const float* lse,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
+    int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  // ---- validation: everything is checked before any CUDA call
+  if (!q || !k || !v || !dout || !out || !lse || !dq || !dk || !dv || !q_strides || !k_strides ||
+      !v_strides)
+    return fail(TT_ATTN_BAD_ARG, "q, k, v, dO, O, LSE, dq, dk, dv and the stride arrays must not "
+                                 "be NULL");
+  if (head_dim != TT_ATTN_HEAD_DIM)
+    return fail(TT_ATTN_BAD_ARG, "attention currently supports only head_dim=64");
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0)
+    return fail(TT_ATTN_BAD_ARG, "attention batch, heads and sequence lengths must be positive");
+  if (past_len < 0) return fail(TT_ATTN_BAD_ARG, "past_len must be non-negative");
+  if (kv_len < q_len || past_len != kv_len - q_len)
+    return fail(TT_ATTN_BAD_ARG, "expected Tk == past_len + Tq");
+  if (q_len > INT32_MAX || kv_len > INT32_MAX)
+    return fail(TT_ATTN_BAD_ARG, "bf16 attention sequence lengths must fit int32 (Tk <= INT32_MAX)");
+  if (batch > INT32_MAX / heads)
+    return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
+  const int64_t bh = batch * heads;
+  const int64_t q_tiles = (q_len + tt::backward::BM - 1) / tt::backward::BM;
+  const int64_t k_tiles = (kv_len + tt::backward::BN - 1) / tt::backward::BN;
+  const int64_t rows = bh * q_len;
+  if (q_tiles > INT32_MAX / bh || k_tiles > INT32_MAX / bh || (rows + 7) / 8 > INT32_MAX)
+    return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
+  const Shape4 qs = canonical(batch, heads, q_len, q_strides);
+  const Shape4 ks = canonical(batch, heads, kv_len, k_strides);
+  const Shape4 vs = canonical(batch, heads, kv_len, v_strides);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !strides_ok(qs.stride) ||
+      !strides_ok(ks.stride) || !strides_ok(vs.stride))
+    return fail(TT_ATTN_UNSUPPORTED,
+                "q/k/v need a unit last stride, other strides in multiples of 8 elements and "
+                "16-byte aligned bases; copy to aligned contiguous storage first");
+  for (const void* ptr : {dout, out, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                          static_cast<const void*>(dv)})
+    if (!aligned16(ptr))
+      return fail(TT_ATTN_BAD_ARG, "dO, O, dq, dk and dv must be contiguous and 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(lse) % 4 != 0)
+    return fail(TT_ATTN_BAD_ARG, "LSE must be 4-byte aligned");
+  const size_t ws_needed = tt_attn_backward_workspace_size(batch, heads, q_len);
+  if (workspace == nullptr || workspace_bytes < ws_needed ||
+      reinterpret_cast<uintptr_t>(workspace) % 4 != 0)
+    return fail(TT_ATTN_BAD_ARG, "workspace is smaller than tt_attn_backward_workspace_size()");
+
+  int dev = 0;
+  tt_attn_status st = prepare_device(&dev);
+  if (st != TT_ATTN_OK) return st;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  float* D = static_cast<float*>(workspace);
+
+  tt::backward::PreParams pp{};
+  pp.rows = rows;
+  pp.dO = static_cast<const __nv_bfloat16*>(dout);
+  pp.O = static_cast<const __nv_bfloat16*>(out);
+  pp.D = D;
+  tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, cs>>>(pp);
+  if ((st = check_launch("bwd_preprocess_kernel launch")) != TT_ATTN_OK) return st;
+
+  const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
+                           TT_ATTN_HEAD_DIM, 1};
+  const Shape4 dos = canonical(batch, heads, q_len, cstr);
+  CUtensorMap tmq, tmk, tmv, tmdo;
+  std::string err;
+  if (!encode_map(&tmq, q, qs, &err) || !encode_map(&tmk, k, ks, &err) ||
+      !encode_map(&tmv, v, vs, &err) || !encode_map(&tmdo, dout, dos, &err))
+    return fail(TT_ATTN_UNSUPPORTED, err);
+
+  tt::backward::Params p{};
+  p.B = static_cast<int>(batch);
+  p.H = static_cast<int>(heads);
+  p.Tq = static_cast<int>(q_len);
+  p.Tk = static_cast<int>(kv_len);
+  p.past_len = static_cast<int>(past_len);
+  p.lse = lse;
+  p.D = D;
+  p.n_tiles = static_cast<int>(q_tiles);
+  p.out0 = static_cast<__nv_bfloat16*>(dq);
+  tt::backward::bwd_dq_kernel<<<static_cast<unsigned>(bh * q_tiles), tt::backward::THREADS,
+                                tt::backward::kSmemQ, cs>>>(tmq, tmk, tmv, tmdo, p);
+  if ((st = check_launch("bwd_dq_kernel launch")) != TT_ATTN_OK) return st;
+  p.n_tiles = static_cast<int>(k_tiles);
+  p.out0 = static_cast<__nv_bfloat16*>(dk);
+  p.out1 = static_cast<__nv_bfloat16*>(dv);
+  tt::backward::bwd_dkdv_kernel<<<static_cast<unsigned>(bh * k_tiles), tt::backward::THREADS,
+                                  tt::backward::kSmemKV, cs>>>(tmq, tmk, tmv, tmdo, p);
+  return check_launch("bwd_dkdv_kernel launch");
 }
 
 TT_ATTN_API tt_attn_status tt_attn_selftest_wait_timeout(int64_t budget_cycles, void* stream) {

@@ -57,11 +57,16 @@ class DecoderConfig:
 
 # ------------------------------------------------------------------------ operators
 
+def _accumulation(x):
+    """FP32 for half-precision tensors, unchanged otherwise (reference.py:12-13)."""
+    return x.float() if x.dtype in (torch.float16, torch.bfloat16) else x
+
+
 def rms_norm(x, weight, eps):
-    """FP32 RMSNorm, output in the input dtype (reference.py:24-27)."""
-    xf = x.float()
+    """RMSNorm in FP32 for half-precision inputs, output in the input dtype (reference.py:24-27)."""
+    xf = _accumulation(x)
     y = xf * torch.rsqrt(xf.square().mean(dim=-1, keepdim=True) + eps)
-    return (y * weight.float()).to(x.dtype)
+    return (y * weight.to(xf.dtype)).to(x.dtype)
 
 
 def rope(x, cos, sin):
@@ -80,8 +85,8 @@ def _causal_allowed(tq, tk, past_len, device):
 def reference_attention(q, k, v, past_len=0):
     """The reference's executable specification (reference.py:49-53), on any device."""
     scores = torch.matmul(q, k.transpose(-1, -2)) / math.sqrt(q.shape[-1])
-    scores = scores.float().masked_fill(~_causal_allowed(q.shape[-2], k.shape[-2], past_len,
-                                                         q.device), float("-inf"))
+    scores = _accumulation(scores).masked_fill(
+        ~_causal_allowed(q.shape[-2], k.shape[-2], past_len, q.device), float("-inf"))
     return torch.matmul(torch.softmax(scores, dim=-1).to(v.dtype), v)
 
 
