@@ -11,17 +11,19 @@
 //
 // Three kernels, in stream order:
 // * bwd_preprocess_kernel: D, one warp per query row (coalesced 128-byte rows).
-// * bwd_dq_kernel: one CTA per (b, h, 128-row query tile), looping over the KV tiles it sees.
-//   tcgen05: S = Q.K^T and dP = dO.V^T (both SS, into TMEM), the elementwise warps (thread =
-//   query row = TMEM lane) turn them into bf16 dS in TMEM, then dQ += dS.K (TS, A from TMEM).
-//   TMEM: S [0,128), dP [128,256), dS [256,320), dQ [320,384).
-// * bwd_dkdv_kernel: one CTA per (b, h, 128-key tile), looping over the query tiles that see
-//   it, in transposed form so that keys are the TMEM lanes: S^T = K.Q^T, dP^T = V.dO^T, the
-//   elementwise warps (thread = key row) write bf16 P^T and dS^T into TMEM, then
-//   dV += P^T.dO and dK += dS^T.Q (TS). Per-query LSE and D come from shared memory
-//   (broadcast reads). TMEM: S^T, dP^T, P^T, dS^T, dV, dK = all 512 columns.
-// Roles in both: warps 0-3 elementwise + epilogue, warp 4 TMA producer (all lanes stage LSE/D
-// in the dK/dV kernel), warp 5 tcgen05 issuer (one thread). Every mbarrier wait is bounded
+// * bwd_dq_kernel: one CTA per (b, h, 128-row query tile), stepping over 64-key tiles.
+//   tcgen05: S = Q.K^T and dP = dO.V^T (SS, M = 128, N = 64, into TMEM); the elementwise warps
+//   (thread = query row = TMEM lane) read them and write bf16 dS over the S columns they have
+//   just read; then dQ += dS.K (TS, A from TMEM). TMEM: S/dS [0,64), dP [64,128), dQ [128,192).
+// * bwd_dkdv_kernel: one CTA per (b, h, 128-key tile), stepping over 64-row query tiles, in
+//   transposed form so that keys are the TMEM lanes: S^T = K.Q^T, dP^T = V.dO^T; the
+//   elementwise warps (thread = key row) write bf16 P^T over S^T and dS^T over dP^T, then
+//   dV += P^T.dO and dK += dS^T.Q (TS). Per-query LSE and D come from shared memory (broadcast
+//   reads). TMEM: S^T/P^T [0,64), dP^T/dS^T [64,128), dV [128,192), dK [192,256).
+// Each step of a CTA is a serial chain (scores -> elementwise -> accumulation). With 256 TMEM
+// columns and ~80 KB of shared memory per CTA, two CTAs share an SM and overlap their chains.
+// Roles: warps 0-3 elementwise + epilogue, warp 4 TMA producer (all lanes stage LSE/D in the
+// dK/dV kernel), warp 5 tcgen05 issuer (one thread). Every mbarrier wait is bounded
 // (TT_ERR_TIMEOUT + abort flag), as in the forward kernels.
 #pragma once
 
@@ -30,25 +32,25 @@
 #include <cstdint>
 
 #include "sm100_ptx.cuh"
-#include "prefill_sm100.cuh"
 
 namespace tt {
 namespace backward {
 
-constexpr int BM = 128;  // query rows per tile
-constexpr int BN = 128;  // keys per tile
+constexpr int TILE = 128;  // rows of the CTA's own tile (UMMA M): query rows or keys
+constexpr int STEP = 64;   // rows of the tile stepped over (UMMA N of the scores)
 constexpr int HD = 64;
 constexpr int STAGES = 3;
 constexpr int THREADS = 192;  // 4 elementwise warps, TMA warp, issuer warp
 constexpr int LOAD_WARP = 4, MMA_WARP = 5;
-constexpr uint32_t TILE_BYTES = 128 * HD * 2;  // 16 KiB
+constexpr uint32_t TILE_BYTES = TILE * HD * 2;  // 16 KiB
+constexpr uint32_t STEP_BYTES = STEP * HD * 2;  // 8 KiB
+constexpr uint32_t TMEM_COLS = 256;
 constexpr float SCALE = 0.125f;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr float LN2 = 0.69314718055994530942f;
 
 struct Params {
   int B, H, Tq, Tk, past_len;
-  int n_tiles;              // query tiles (dQ kernel) or key tiles (dK/dV kernel)
+  int n_tiles;              // query tiles (dQ kernel) or key tiles (dK/dV kernel) of TILE rows
   const float* lse;         // contiguous [B, H, Tq], natural log
   const float* D;           // contiguous [B, H, Tq]
   __nv_bfloat16* out0;      // dQ (dQ kernel) or dK (dK/dV kernel), contiguous
@@ -79,8 +81,8 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const PreParams p) 
 struct alignas(1024) SmemQ {  // dQ kernel
   uint8_t q[TILE_BYTES];
   uint8_t dO[TILE_BYTES];
-  uint8_t k[STAGES][TILE_BYTES];
-  uint8_t v[STAGES][TILE_BYTES];
+  uint8_t k[STAGES][STEP_BYTES];
+  uint8_t v[STAGES][STEP_BYTES];
   uint64_t qd_full;
   uint64_t kv_full[STAGES], kv_empty[STAGES];
   uint64_t s_full, s_free, ds_ready, dq_done, drain;
@@ -91,10 +93,10 @@ struct alignas(1024) SmemQ {  // dQ kernel
 struct alignas(1024) SmemKV {  // dK/dV kernel
   uint8_t k[TILE_BYTES];
   uint8_t v[TILE_BYTES];
-  uint8_t q[STAGES][TILE_BYTES];
-  uint8_t dO[STAGES][TILE_BYTES];
-  float lse2[STAGES][BM];  // LSE * log2(e) per query row of the stage (+inf past Tq)
-  float d[STAGES][BM];
+  uint8_t q[STAGES][STEP_BYTES];
+  uint8_t dO[STAGES][STEP_BYTES];
+  float lse2[STAGES][STEP];  // LSE * log2(e) per query row of the stage (+inf past Tq)
+  float d[STAGES][STEP];
   uint64_t kv_full;
   uint64_t q_full[STAGES], q_empty[STAGES];
   uint64_t st_full, st_free, pd_ready, acc_done, drain;
@@ -104,6 +106,8 @@ struct alignas(1024) SmemKV {  // dK/dV kernel
 
 constexpr size_t kSmemQ = sizeof(SmemQ) + 1024;
 constexpr size_t kSmemKV = sizeof(SmemKV) + 1024;
+static_assert(2 * kSmemQ <= 228 * 1024 && 2 * kSmemKV <= 228 * 1024,
+              "two CTAs per SM must fit in shared memory");
 
 template <class S>
 __device__ __forceinline__ bool wait_or_abort(S& s, uint64_t* bar, uint32_t parity) {
@@ -127,17 +131,25 @@ __device__ __forceinline__ bool warp_wait(S& s, uint64_t* bar, uint32_t parity) 
   return __all_sync(0xffffffffu, ok);
 }
 
-// KV tiles (of BN keys) that query rows [q0, q0 + BM) see.
-__device__ __forceinline__ int kv_tiles_seen(const Params& p, int q0) {
-  const long long end =
-      min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + BM + p.past_len);
-  return static_cast<int>((end + BN - 1) / BN);
+// D = A.B^T with A, B both K-major 128-byte-swizzled tiles of 64 features (4 k-steps of 16).
+__device__ __forceinline__ void issue_scores(uint32_t tmem_d, uint32_t a_addr, uint32_t b_addr,
+                                             uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk)
+    umma_ss(tmem_d, make_sdesc_sw128(a_addr + kk * 32, 16, 1024),
+            make_sdesc_sw128(b_addr + kk * 32, 16, 1024), idesc, kk > 0 ? 1u : 0u);
 }
 
-// First query tile whose rows see key tile kt (keys [BN kt, BN kt + BN)).
-__device__ __forceinline__ int first_q_tile(const Params& p, int kt) {
-  const long long q_first = max(0LL, static_cast<long long>(kt) * BN - p.past_len);
-  return static_cast<int>(q_first / BM);
+// D += A.B with A = bf16 pairs in TMEM over STEP rows of K, laid out by the elementwise warps
+// as chunk c (K rows [32c, 32c + 32)) at TMEM columns [32c, 32c + 16) of its region; B = a
+// STEP x 64 tile, MN-major (16 K rows x 128 B = 2048 B per k-step).
+__device__ __forceinline__ void issue_accumulate(uint32_t tmem_d, uint32_t tmem_a, uint32_t b_addr,
+                                                 uint32_t idesc, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < STEP / 16; ++kk)
+    umma_ts(tmem_d, tmem_a + 32 * (kk >> 1) + 8 * (kk & 1),
+            make_sdesc_sw128(b_addr + kk * 2048, 8192, 1024), idesc,
+            (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_t (&acc)[32],
@@ -154,7 +166,7 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_
 }
 
 // ------------------------------------------------------------------ dQ kernel
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
 bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
               const Params p) {
@@ -166,9 +178,11 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   const int qt = p.n_tiles - 1 - static_cast<int>(blockIdx.x / BH);  // heaviest tiles first
   const int bh = static_cast<int>(blockIdx.x % BH);
   const int b = bh / p.H, h = bh % p.H;
-  const int q0 = qt * BM;
-  const int n_kv = kv_tiles_seen(p, q0);
-  constexpr uint32_t T_S = 0, T_DP = 128, T_DS = 256, T_DQ = 320;
+  const int q0 = qt * TILE;
+  const long long kend =
+      min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + TILE + p.past_len);
+  const int n_kv = static_cast<int>((kend + STEP - 1) / STEP);  // key steps this tile sees
+  constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.qd_full, 1);
@@ -185,7 +199,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     fence_barrier_init();
   }
   if (warp == MMA_WARP) {
-    tmem_alloc(&s.tmem_base, 512);
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -202,9 +216,9 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       for (int j = 0; j < n_kv; ++j) {
         const int st = j % STAGES;
         if (j >= STAGES && !wait_or_abort(s, &s.kv_empty[st], ((j / STAGES) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&s.kv_full[st], 2 * TILE_BYTES);
-        tma_load_4d(s.k[st], &tm_k, &s.kv_full[st], 0, j * BN, h, b);
-        tma_load_4d(s.v[st], &tm_v, &s.kv_full[st], 0, j * BN, h, b);
+        mbar_arrive_expect_tx(&s.kv_full[st], 2 * STEP_BYTES);
+        tma_load_4d(s.k[st], &tm_k, &s.kv_full[st], 0, j * STEP, h, b);
+        tma_load_4d(s.v[st], &tm_v, &s.kv_full[st], 0, j * STEP, h, b);
         issued = j + 1;
       }
       if (s.abort) {
@@ -215,8 +229,8 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     }
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
-      const uint32_t idesc_s = make_idesc_bf16(BM, BN, false);
-      const uint32_t idesc_o = make_idesc_bf16(BM, HD, true);
+      const uint32_t idesc_s = make_idesc_bf16(TILE, STEP, false);
+      const uint32_t idesc_o = make_idesc_bf16(TILE, HD, true);
       const uint32_t q_addr = smem_u32(s.q), do_addr = smem_u32(s.dO);
       bool ok = wait_or_abort(s, &s.qd_full, 0);
       for (int j = 0; ok && j < n_kv; ++j) {
@@ -224,12 +238,12 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         if (!wait_or_abort(s, &s.kv_full[st], (j / STAGES) & 1)) break;
         if (j > 0 && !wait_or_abort(s, &s.s_free, (j - 1) & 1)) break;
         tc_fence_after();
-        prefill::issue_s_mma(tmem + T_S, q_addr, smem_u32(s.k[st]), idesc_s);
-        prefill::issue_s_mma(tmem + T_DP, do_addr, smem_u32(s.v[st]), idesc_s);
+        issue_scores(tmem + T_S, q_addr, smem_u32(s.k[st]), idesc_s);
+        issue_scores(tmem + T_DP, do_addr, smem_u32(s.v[st]), idesc_s);
         umma_commit(&s.s_full);
         if (!wait_or_abort(s, &s.ds_ready, j & 1)) break;
         tc_fence_after();
-        prefill::issue_pv_mma(tmem + T_DQ, tmem + T_DS, smem_u32(s.k[st]), idesc_o, j > 0);
+        issue_accumulate(tmem + T_DQ, tmem + T_S, smem_u32(s.k[st]), idesc_o, j > 0);
         umma_commit(&s.dq_done);
         umma_commit(&s.kv_empty[st]);
       }
@@ -251,12 +265,13 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!warp_wait(s, &s.s_full, j & 1)) { ok = false; break; }
+      // dS overwrites S, which the previous dQ += dS.K may still be reading.
       if (j > 0 && !warp_wait(s, &s.dq_done, (j - 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      const long long kv0 = static_cast<long long>(j) * BN;
-      const bool masked = kv0 + BN - 1 > tile_limit;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      const long long kv0 = static_cast<long long>(j) * STEP;
+      const bool masked = kv0 + STEP - 1 > tile_limit;
+#pragma unroll
+      for (int c = 0; c < STEP / 32; ++c) {
         uint32_t sr[32], dr[32];
         tmem_ld32(tmem + lane_base + T_S + c * 32, sr);
         tmem_ld32(tmem + lane_base + T_DP + c * 32, dr);
@@ -266,18 +281,17 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         uint32_t ds[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float pv[2], dv[2];
+          float dv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int col = 2 * e + u;
             float pp = ex2_approx(__uint_as_float(sr[col]) * sl2 - lse2);
             if (masked && kv0 + c * 32 + col > row_limit) pp = 0.f;
-            pv[u] = pp;
             dv[u] = pp * (__uint_as_float(dr[col]) - drow);
           }
           ds[e] = pack_bf16x2(dv[0], dv[1]);
         }
-        tmem_st16(tmem + lane_base + T_DS + c * 16, ds);
+        tmem_st16(tmem + lane_base + T_S + c * 32, ds);  // over S columns this thread has read
       }
       tmem_wait_st();
       tc_fence_before();
@@ -305,12 +319,12 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   if (warp == MMA_WARP) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
 // ------------------------------------------------------------------ dK/dV kernel
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
 bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const Params p) {
@@ -322,10 +336,12 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   const int kt = static_cast<int>(blockIdx.x / BH);  // low key tiles see the most queries
   const int bh = static_cast<int>(blockIdx.x % BH);
   const int b = bh / p.H, h = bh % p.H;
-  const int k0 = kt * BN;
-  const int qt0 = first_q_tile(p, kt);
-  const int n_q = (p.Tq + BM - 1) / BM - qt0;  // >= 1: the last query row sees every key
-  constexpr uint32_t T_ST = 0, T_DPT = 128, T_PT = 256, T_DST = 320, T_DV = 384, T_DK = 448;
+  const int k0 = kt * TILE;
+  // Query steps (of STEP rows) that see some key of this tile: from the step holding query
+  // k0 - past_len on; the last query row sees every key, so there is at least one.
+  const int qs0 = static_cast<int>(max(0LL, static_cast<long long>(k0) - p.past_len) / STEP);
+  const int n_q = (p.Tq + STEP - 1) / STEP - qs0;
+  constexpr uint32_t T_ST = 0, T_DPT = 64, T_DV = 128, T_DK = 192;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.kv_full, 1);
@@ -342,7 +358,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     fence_barrier_init();
   }
   if (warp == MMA_WARP) {
-    tmem_alloc(&s.tmem_base, 512);
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -359,12 +375,12 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     }
     for (int i = 0; i < n_q; ++i) {
       const int st = i % STAGES;
-      const int q0 = (qt0 + i) * BM;
+      const int q0 = (qs0 + i) * STEP;
       if (i >= STAGES && !warp_wait(s, &s.q_empty[st], ((i / STAGES) - 1) & 1)) break;
-      // Per-query LSE (log2 units) and D of this tile; rows past Tq get +inf / 0, so their
+      // Per-query LSE (log2 units) and D of this step; rows past Tq get +inf / 0, so their
       // probabilities are exactly zero.
 #pragma unroll
-      for (int e = 0; e < BM / 32; ++e) {
+      for (int e = 0; e < STEP / 32; ++e) {
         const int rr = e * 32 + lane;
         const int q = q0 + rr;
         const size_t idx = static_cast<size_t>(bh) * p.Tq + static_cast<size_t>(q);
@@ -373,7 +389,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive_expect_tx(&s.q_full[st], 2 * TILE_BYTES);
+        mbar_arrive_expect_tx(&s.q_full[st], 2 * STEP_BYTES);
         tma_load_4d(s.q[st], &tm_q, &s.q_full[st], 0, q0, h, b);
         tma_load_4d(s.dO[st], &tm_do, &s.q_full[st], 0, q0, h, b);
       }
@@ -386,8 +402,8 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     }
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
-      const uint32_t idesc_s = make_idesc_bf16(BN, BM, false);
-      const uint32_t idesc_o = make_idesc_bf16(BN, HD, true);
+      const uint32_t idesc_s = make_idesc_bf16(TILE, STEP, false);
+      const uint32_t idesc_o = make_idesc_bf16(TILE, HD, true);
       const uint32_t k_addr = smem_u32(s.k), v_addr = smem_u32(s.v);
       bool ok = wait_or_abort(s, &s.kv_full, 0);
       for (int i = 0; ok && i < n_q; ++i) {
@@ -395,13 +411,13 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         if (!wait_or_abort(s, &s.q_full[st], (i / STAGES) & 1)) break;
         if (i > 0 && !wait_or_abort(s, &s.st_free, (i - 1) & 1)) break;
         tc_fence_after();
-        prefill::issue_s_mma(tmem + T_ST, k_addr, smem_u32(s.q[st]), idesc_s);
-        prefill::issue_s_mma(tmem + T_DPT, v_addr, smem_u32(s.dO[st]), idesc_s);
+        issue_scores(tmem + T_ST, k_addr, smem_u32(s.q[st]), idesc_s);
+        issue_scores(tmem + T_DPT, v_addr, smem_u32(s.dO[st]), idesc_s);
         umma_commit(&s.st_full);
         if (!wait_or_abort(s, &s.pd_ready, i & 1)) break;
         tc_fence_after();
-        prefill::issue_pv_mma(tmem + T_DV, tmem + T_PT, smem_u32(s.dO[st]), idesc_o, i > 0);
-        prefill::issue_pv_mma(tmem + T_DK, tmem + T_DST, smem_u32(s.q[st]), idesc_o, i > 0);
+        issue_accumulate(tmem + T_DV, tmem + T_ST, smem_u32(s.dO[st]), idesc_o, i > 0);
+        issue_accumulate(tmem + T_DK, tmem + T_DPT, smem_u32(s.q[st]), idesc_o, i > 0);
         umma_commit(&s.acc_done);
         umma_commit(&s.q_empty[st]);
       }
@@ -417,14 +433,15 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     bool ok = true;
     for (int i = 0; i < n_q; ++i) {
       const int st = i % STAGES;
-      const long long q0 = static_cast<long long>(qt0 + i) * BM;
+      const long long q0 = static_cast<long long>(qs0 + i) * STEP;
       if (!warp_wait(s, &s.st_full, i & 1)) { ok = false; break; }
+      // P^T / dS^T overwrite S^T / dP^T, which the previous accumulation may still read.
       if (i > 0 && !warp_wait(s, &s.acc_done, (i - 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      // Pair (key, q) is visible iff key <= q + past_len; only tiles crossing the diagonal mask.
-      const bool masked = static_cast<long long>(k0) + BN - 1 > q0 + p.past_len;
-#pragma unroll 1
-      for (int c = 0; c < BM / 32; ++c) {
+      // Pair (key, q) is visible iff key <= q + past_len; only steps crossing the diagonal mask.
+      const bool masked = static_cast<long long>(k0) + TILE - 1 > q0 + p.past_len;
+#pragma unroll
+      for (int c = 0; c < STEP / 32; ++c) {
         uint32_t sr[32], dr[32];
         tmem_ld32(tmem + lane_base + T_ST + c * 32, sr);
         tmem_ld32(tmem + lane_base + T_DPT + c * 32, dr);
@@ -447,8 +464,8 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           pk[e] = pack_bf16x2(pv[0], pv[1]);
           ds[e] = pack_bf16x2(dv[0], dv[1]);
         }
-        tmem_st16(tmem + lane_base + T_PT + c * 16, pk);
-        tmem_st16(tmem + lane_base + T_DST + c * 16, ds);
+        tmem_st16(tmem + lane_base + T_ST + c * 32, pk);   // over S^T columns just read
+        tmem_st16(tmem + lane_base + T_DPT + c * 32, ds);  // over dP^T columns just read
       }
       tmem_wait_st();
       tc_fence_before();
@@ -481,7 +498,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   if (warp == MMA_WARP) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 

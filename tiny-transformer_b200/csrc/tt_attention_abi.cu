@@ -352,8 +352,8 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   if (batch > INT32_MAX / heads)
     return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
   const int64_t bh = batch * heads;
-  const int64_t q_tiles = (q_len + tt::backward::BM - 1) / tt::backward::BM;
-  const int64_t k_tiles = (kv_len + tt::backward::BN - 1) / tt::backward::BN;
+  const int64_t q_tiles = (q_len + tt::backward::TILE - 1) / tt::backward::TILE;
+  const int64_t k_tiles = (kv_len + tt::backward::TILE - 1) / tt::backward::TILE;
   const int64_t rows = bh * q_len;
   if (q_tiles > INT32_MAX / bh || k_tiles > INT32_MAX / bh || (rows + 7) / 8 > INT32_MAX)
     return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
@@ -393,10 +393,15 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
                            TT_ATTN_HEAD_DIM, 1};
   const Shape4 dos = canonical(batch, heads, q_len, cstr);
-  CUtensorMap tmq, tmk, tmv, tmdo;
+  // The dQ kernel reads Q / dO in 128-row tiles and K / V in 64-row steps; the dK/dV kernel
+  // the other way round.
+  constexpr unsigned tile = tt::backward::TILE, step = tt::backward::STEP;
+  CUtensorMap tmq_t, tmdo_t, tmk_s, tmv_s, tmq_s, tmdo_s, tmk_t, tmv_t;
   std::string err;
-  if (!encode_map(&tmq, q, qs, &err) || !encode_map(&tmk, k, ks, &err) ||
-      !encode_map(&tmv, v, vs, &err) || !encode_map(&tmdo, dout, dos, &err))
+  if (!encode_map(&tmq_t, q, qs, &err, tile) || !encode_map(&tmdo_t, dout, dos, &err, tile) ||
+      !encode_map(&tmk_s, k, ks, &err, step) || !encode_map(&tmv_s, v, vs, &err, step) ||
+      !encode_map(&tmq_s, q, qs, &err, step) || !encode_map(&tmdo_s, dout, dos, &err, step) ||
+      !encode_map(&tmk_t, k, ks, &err, tile) || !encode_map(&tmv_t, v, vs, &err, tile))
     return fail(TT_ATTN_UNSUPPORTED, err);
 
   tt::backward::Params p{};
@@ -410,13 +415,13 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   p.n_tiles = static_cast<int>(q_tiles);
   p.out0 = static_cast<__nv_bfloat16*>(dq);
   tt::backward::bwd_dq_kernel<<<static_cast<unsigned>(bh * q_tiles), tt::backward::THREADS,
-                                tt::backward::kSmemQ, cs>>>(tmq, tmk, tmv, tmdo, p);
+                                tt::backward::kSmemQ, cs>>>(tmq_t, tmk_s, tmv_s, tmdo_t, p);
   if ((st = check_launch("bwd_dq_kernel launch")) != TT_ATTN_OK) return st;
   p.n_tiles = static_cast<int>(k_tiles);
   p.out0 = static_cast<__nv_bfloat16*>(dk);
   p.out1 = static_cast<__nv_bfloat16*>(dv);
   tt::backward::bwd_dkdv_kernel<<<static_cast<unsigned>(bh * k_tiles), tt::backward::THREADS,
-                                  tt::backward::kSmemKV, cs>>>(tmq, tmk, tmv, tmdo, p);
+                                  tt::backward::kSmemKV, cs>>>(tmq_s, tmk_t, tmv_t, tmdo_s, p);
   return check_launch("bwd_dkdv_kernel launch");
 }
 
