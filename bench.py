@@ -269,7 +269,44 @@ def run_ours(args):
                      "ms_per_step": round(sdpa_ms, 4)},
             "clocks": clk.summary(),
         }
-        del q, k, v, hq, hk, hv, ho, hl
+        del hq, hk, hv, ho, hl
+
+        # ------------------------------------------------------------------ backward (cfg 3)
+        # dQ, dK, dV of the same prefill (the training path of student.attention); work counted
+        # as 2.5x the forward FLOPs (five GEMMs: QK^T recomputed, dO.V^T, P^T.dO, dS^T.Q, dS.K).
+        out, lse = ext.attention_forward(q, k, v, 0)
+        g = torch.Generator(device="cuda").manual_seed(77 + rank)
+        dout = torch.randn(q.shape, device="cuda", dtype=torch.bfloat16, generator=g)
+        bwd_flops = 2.5 * flops
+        bsteps = max(3, args.steps // 2)
+        fn = lambda: ext.attention_backward(q, k, v, dout, out, lse, 0)  # noqa: E731
+        barrier(world)
+        torch.cuda.synchronize()
+        times = time_device(torch, fn, bsteps, args.warmup, flush)
+        barrier(world)
+        torch.cuda.synchronize()
+        bwd_ms = reduce_max(sum(times) / len(times), world)
+        with torch.enable_grad():
+            qq, kk, vv = [x.detach().requires_grad_() for x in (q, k, v)]
+            o2 = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True)
+            sd = lambda: torch.autograd.grad(o2, (qq, kk, vv), dout, retain_graph=True)  # noqa: E731
+            sdpa_bwd_ms = sum(time_device(torch, sd, bsteps, args.warmup, flush)) / bsteps
+            del qq, kk, vv, o2
+        results["backward"] = {
+            "metric": "causal attn bwd TFLOP/s (2.5x forward FLOPs)",
+            "value": round(world * bwd_flops / (bwd_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(bwd_ms, 4),
+            "config": {"workload": "cfg3 backward (dQ, dK, dV) B=4 H=12 Tq=Tk=4096 D=64 bf16, "
+                                   "per rank", "algorithmic_flops": bwd_flops},
+            "roofline": {"bound": "tensor",
+                         "achieved": round(bwd_flops / (bwd_ms * 1e-3) / 1e12, 2),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(bwd_flops / (bwd_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)},
+            "gpu_launches": 3 * bsteps,
+            "sdpa": {"value": round(bwd_flops / (sdpa_bwd_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                     "ms_per_step": round(sdpa_bwd_ms, 4)},
+        }
+        del q, k, v, out, lse, dout
 
         # ------------------------------------------------------------------ decode (cfg 4)
         c = DECODE_CFG
@@ -345,6 +382,7 @@ def run_ours(args):
     if "sdpa" in head:
         line["sdpa"] = head["sdpa"]
     line[other_key] = results[other_key]
+    line["backward"] = results["backward"]
     print(json.dumps(line), flush=True)
 
 

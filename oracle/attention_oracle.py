@@ -121,6 +121,28 @@ def attention_fp64(q: np.ndarray, k: np.ndarray, v: np.ndarray, past_len: int = 
     return out, lse
 
 
+def attention_backward_fp64(q: np.ndarray, k: np.ndarray, v: np.ndarray, dout: np.ndarray,
+                            past_len: int = 0):
+    """FP64 gradients of attention_fp64 with respect to q, k, v for upstream ``dout``, in the
+    form of the reference's BF16 backward (csrc/attention/attention.cu:161-234 with
+    attention_backward_preprocess_kernel.cuh, attention_backward_dKdV_kernel.cu:232-309 and
+    attention_backward_dQ_kernel.cu): D = rowsum(dO * O), P = exp(S / 8 - LSE) on visible
+    pairs, dS = P * (dO.V^T - D), dQ = dS.K / 8, dK = dS^T.Q / 8, dV = P^T.dO. Returns
+    (dQ, dK, dV), FP64."""
+    _check(q, k, v, past_len)
+    q, k, v, dout = (np.asarray(x, dtype=np.float64) for x in (q, k, v, dout))
+    out, lse = attention_fp64(q, k, v, past_len)
+    allowed = causal_allowed(q.shape[2], k.shape[2], past_len)
+    scores = np.matmul(q, np.swapaxes(k, -1, -2)) / 8.0
+    p = np.where(allowed, np.exp(scores - lse[..., None]), 0.0)
+    d = (dout * out).sum(axis=-1, keepdims=True)
+    ds = p * (np.matmul(dout, np.swapaxes(v, -1, -2)) - d)
+    dq = np.matmul(ds, k) / 8.0
+    dk = np.matmul(np.swapaxes(ds, -1, -2), q) / 8.0
+    dv = np.matmul(np.swapaxes(p, -1, -2), dout)
+    return dq, dk, dv
+
+
 def decode_with_kv_lens(q: np.ndarray, k: np.ndarray, v: np.ndarray, kv_lens, fn=attention_fp64):
     """Single-token decode where key j is visible to batch row b iff j < kv_lens[b].
 

@@ -120,3 +120,23 @@ def test_bf16_rounding(x):
         assert abs(r - x) <= max(abs(x) * 2 ** -8, 2.0 ** -133)  # subnormals: absolute
     else:
         assert r == x or np.isinf(r)
+
+
+def test_oracle_backward_matches_fp64_autograd():
+    """The FP64 backward restatement equals torch autograd of the FP64 forward, including a
+    chunked-prefill (past_len > 0) case and rows whose keys are partly masked."""
+    import torch
+    from oracle import attention_oracle as oracle
+    g = torch.Generator().manual_seed(21)
+    for tq, tk in ((9, 9), (5, 12), (1, 7)):
+        q, k, v, dout = (torch.randn(2, 3, t, 64, generator=g, dtype=torch.float64)
+                         for t in (tq, tk, tk, tq))
+        past = tk - tq
+        qq, kk, vv = (x.clone().requires_grad_() for x in (q, k, v))
+        mask = torch.arange(tk)[None, :] <= torch.arange(tq)[:, None] + past
+        scores = (qq @ kk.transpose(-1, -2) / 8).masked_fill(~mask, float("-inf"))
+        out = scores.softmax(-1) @ vv
+        want = torch.autograd.grad(out, (qq, kk, vv), dout)
+        got = oracle.attention_backward_fp64(q.numpy(), k.numpy(), v.numpy(), dout.numpy(), past)
+        for a, b in zip(got, want):
+            np.testing.assert_allclose(a, b.numpy(), rtol=1e-10, atol=1e-12)
