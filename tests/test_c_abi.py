@@ -97,3 +97,38 @@ def test_workspace_and_layout_queries(lib):
     assert lib.tt_attn_layout_supported(16, _strides(4096, 4096, 64, 2)) == 0
     assert lib.tt_attn_layout_supported(16, _strides(0, 4096, 64, 1)) == 0
     assert lib.tt_attn_layout_supported(None, _strides(4096, 4096, 64, 1)) == 0
+
+
+def _bwd(lib, *, q=16, k=16, v=16, do=16, o=16, lse=16, dq=16, dk=16, dv=16, B=1, H=1, tq=4,
+         tk=4, d=64, past=0, ws=256, ws_bytes=1 << 20):
+    qs = _strides(tq * 64 * H, tq * 64, 64, 1)
+    ks = _strides(tk * 64 * H, tk * 64, 64, 1)
+    return lib.tt_attn_backward_bf16(q, qs, k, ks, v, ks, do, o, lse, B, H, tq, tk, d, past,
+                                     dq, dk, dv, ws, ws_bytes, None)
+
+
+@pytest.mark.parametrize("kwargs,fragment", [
+    (dict(do=None), "must not"),
+    (dict(d=32), "head_dim=64"),
+    (dict(B=0), "positive"),
+    (dict(past=-1), "non-negative"),
+    (dict(tk=5), "Tk == past_len + Tq"),
+    (dict(tq=2**31, tk=2**31), "int32"),
+    (dict(B=2**20, H=2**12), "grid limits"),
+    (dict(dq=24), "16-byte"),
+    (dict(lse=18), "4-byte"),
+    (dict(ws_bytes=4), "workspace"),
+])
+def test_backward_rejects_bad_arguments_before_cuda(lib, kwargs, fragment):
+    assert _bwd(lib, **kwargs) == 1  # TT_ATTN_BAD_ARG
+    assert fragment in _err(lib)
+
+
+def test_backward_unsupported_layout_and_workspace_size(lib):
+    # q with a feature stride of 2 cannot be read in place.
+    qs = _strides(4 * 128, 128, 128, 2)
+    ks = _strides(4 * 64, 64, 64, 1)
+    assert lib.tt_attn_backward_bf16(16, qs, 16, ks, 16, ks, 16, 16, 16, 1, 1, 4, 4, 64, 0,
+                                     16, 16, 16, 256, 1 << 20, None) == 2  # UNSUPPORTED
+    assert lib.tt_attn_backward_workspace_size(2, 3, 5) == 2 * 3 * 5 * 4
+    assert lib.tt_attn_backward_workspace_size(0, 3, 5) == 0

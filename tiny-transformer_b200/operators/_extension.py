@@ -52,6 +52,15 @@ def load_c_abi() -> ctypes.CDLL:
     lib.tt_attn_device_supported.argtypes = []
     lib.tt_attn_device_status.restype = ctypes.c_int
     lib.tt_attn_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
+    lib.tt_attn_backward_bf16.restype = ctypes.c_int
+    lib.tt_attn_backward_bf16.argtypes = [
+        ctypes.c_void_p, i64p, ctypes.c_void_p, i64p, ctypes.c_void_p, i64p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.c_void_p]
+    lib.tt_attn_backward_workspace_size.restype = ctypes.c_size_t
+    lib.tt_attn_backward_workspace_size.argtypes = [ctypes.c_int64] * 3
     lib.tt_rope_append_bf16.restype = ctypes.c_int
     lib.tt_rope_append_bf16.argtypes = [
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
