@@ -549,6 +549,12 @@ def run_profile_case(which):
             q, k, v = make_prefill(torch, 0)
             for _ in range(3):
                 ext.attention_forward(q, k, v, 0)
+        elif which == "backward":
+            q, k, v = make_prefill(torch, 0)
+            out, lse = ext.attention_forward(q, k, v, 0)
+            dout = torch.randn_like(out)
+            for _ in range(3):
+                ext.attention_backward(q, k, v, dout, out, lse, 0)
         else:
             q, k, v, lens = make_decode(torch, 0)
             for _ in range(3):
@@ -565,7 +571,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("prefill", "decode", "generation"), default="prefill")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
-    ap.add_argument("--profile", choices=("prefill", "decode"), default=None,
+    ap.add_argument("--profile", choices=("prefill", "decode", "backward"), default=None,
                     help="run 3 launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
