@@ -10,7 +10,7 @@
 // with key j visible to query i iff j <= i + past_len (Tk == Tq + past_len), scale = 1/8.
 //
 // Three kernels, in stream order:
-// * bwd_preprocess_kernel: D, one warp per query row (coalesced 128-byte rows).
+// * bwd_preprocess_kernel: D, eight lanes per query row (16-byte loads of dO and O).
 // * bwd_dq_kernel: one CTA per (b, h, 128-row query tile), stepping over 64-key tiles.
 //   tcgen05: S = Q.K^T and dP = dO.V^T (SS, M = 128, N = 64, into TMEM); the elementwise warps
 //   (thread = query row = TMEM lane) read them and write bf16 dS over the S columns they have
@@ -65,16 +65,26 @@ struct PreParams {
   float* D;
 };
 
+// Eight lanes per row, 16-byte loads: a warp covers four rows, a block of 256 threads 32.
+constexpr int PRE_ROWS_PER_BLOCK = 32;
+
 __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const PreParams p) {
-  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= p.rows) return;
-  const uint32_t a = reinterpret_cast<const uint32_t*>(p.dO + row * HD)[lane];
-  const uint32_t o = reinterpret_cast<const uint32_t*>(p.O + row * HD)[lane];
-  float sum = bf16_lo(a) * bf16_lo(o) + bf16_hi(a) * bf16_hi(o);
+  const long long row =
+      static_cast<long long>(blockIdx.x) * PRE_ROWS_PER_BLOCK + (threadIdx.x >> 3);
+  const int part = threadIdx.x & 7;  // 8 features per lane
+  float sum = 0.f;
+  if (row < p.rows) {
+    const uint4 a = reinterpret_cast<const uint4*>(p.dO + row * HD)[part];
+    const uint4 o = reinterpret_cast<const uint4*>(p.O + row * HD)[part];
+    sum = bf16_lo(a.x) * bf16_lo(o.x) + bf16_hi(a.x) * bf16_hi(o.x) +
+          bf16_lo(a.y) * bf16_lo(o.y) + bf16_hi(a.y) * bf16_hi(o.y) +
+          bf16_lo(a.z) * bf16_lo(o.z) + bf16_hi(a.z) * bf16_hi(o.z) +
+          bf16_lo(a.w) * bf16_lo(o.w) + bf16_hi(a.w) * bf16_hi(o.w);
+  }
+  // Reduce over the eight lanes of the row (all 32 lanes take part in every shuffle).
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  if (lane == 0) p.D[row] = sum;
+  for (int off = 4; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (part == 0 && row < p.rows) p.D[row] = sum;
 }
 
 // ------------------------------------------------------------------ shared pieces

@@ -387,7 +387,9 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   pp.dO = static_cast<const __nv_bfloat16*>(dout);
   pp.O = static_cast<const __nv_bfloat16*>(out);
   pp.D = D;
-  tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, cs>>>(pp);
+  const int64_t pre_blocks =
+      (rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK;
+  tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>(pre_blocks), 256, 0, cs>>>(pp);
   if ((st = check_launch("bwd_preprocess_kernel launch")) != TT_ATTN_OK) return st;
 
   const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
