@@ -14,7 +14,7 @@ onto this path, checked against the CPU oracle (oracle/attention_oracle.py):
   answer is 1), a result that is at least as close to the FP64 answer as the reference passes.
 
 Tile-boundary cases are widened from the reference's 64-row tiles to this kernel's 128-row query
-tiles, 128-key KV tiles and 64/128/256-key decode chunks. Everything calls through the native
+tiles, 128-key KV tiles, 384-key decode ring stages and 384/768/1536-key decode work items. Everything calls through the native
 extension, which calls the C ABI (tt_attn_forward_bf16).
 """
 import math
@@ -266,9 +266,12 @@ def test_unaligned_and_strided_views(ext):
 
 
 def test_decode_split_boundaries_and_rescaling(ext):
-    # reference :289-310, boundaries of 64/128/256-key chunks and long caches.
-    for tk in (1, 2, 7, 63, 64, 65, 127, 128, 129, 255, 256, 257, 511, 512, 513, 4095, 4096, 4097,
-               8192, 8193):
+    # reference :289-310, boundaries of 32-row warp slices, 384-key ring stages (the two-stage
+    # ring wraps at 768) and 384-key work items (six heads always take the smallest item),
+    # and long caches.
+    for tk in (1, 2, 7, 31, 32, 33, 63, 64, 65, 127, 128, 129, 255, 256, 257, 383, 384, 385,
+               511, 512, 513, 767, 768, 769, 1151, 1152, 1153, 1535, 1536, 1537, 3072, 3073,
+               4095, 4096, 4097, 8192, 8193):
         q = torch.randn(2, 3, 1, 64, device="cuda", dtype=torch.bfloat16)
         k, v = [torch.randn(2, 3, tk, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
         check_forward(ext, q, k, v, tk - 1)
@@ -431,12 +434,32 @@ def test_rejects_sequence_index_overflow_before_copy(ext):
             ext.attention_forward(q, kv, kv, tk - tq)
 
 
+@pytest.mark.parametrize("tk,chunk", [(769, 768), (1536, 768), (1537, 1536), (3073, 1536),
+                                      (4608, 1536)])
+def test_decode_work_item_sizes(ext, tk, chunk):
+    """Enough heads (50 x 12) that the host picks 768- and 1536-key work items: sequence ends on
+    and beside item boundaries, with and without kv_lens. The chosen item size is read back
+    from the workspace the C ABI asks for (a counter plus one 272-byte partial per item)."""
+    from tiny_transformer_b200.operators._extension import load_c_abi
+    B, H = 50, 12
+    n_items = -(-tk // chunk)
+    assert load_c_abi().tt_attn_forward_workspace_size(B, H, 1, tk) == 256 + B * H * n_items * 272
+    torch.manual_seed(tk)
+    q = torch.randn(B, H, 1, 64, device="cuda", dtype=torch.bfloat16)
+    k, v = [torch.randn(B, H, tk, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    check_forward(ext, q, k, v, tk - 1, sdpa=False)
+    edges = [1, chunk - 1, chunk, chunk + 1, tk - 1, tk, 2 * chunk + 1, 0]
+    lens = torch.tensor([edges[b % len(edges)] for b in range(B)], dtype=torch.int32)
+    check_forward(ext, q, k, v, tk - 1, kv_lens=lens.cuda())
+
+
 # ----------------------------------------------------------------------------- kv_lens (new)
 def test_kv_lens_masks_beyond_length(ext):
     """Key j visible iff j < kv_lens[b]: NaN-poisoned cache beyond each length, lengths on chunk
     boundaries, 0 (O = 0, LSE = -inf) and > Tk (clamped)."""
-    tk = 1100
-    lens_list = [1, 63, 64, 65, 255, 256, 257, 1000, 1100, 0, 5000, 700]
+    tk = 1600
+    lens_list = [1, 63, 64, 65, 383, 384, 385, 767, 768, 769, 0, 1535, 1536, 1537, 1600, 5000,
+                 700]
     B = len(lens_list)
     q = torch.randn(B, 2, 1, 64, device="cuda", dtype=torch.bfloat16)
     k = torch.randn(B, 2, tk, 64, device="cuda", dtype=torch.bfloat16)
@@ -449,7 +472,8 @@ def test_kv_lens_masks_beyond_length(ext):
         out, lse = ext.attention_forward(q, k, v, tk - 1, None, lens)
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
-        assert (out[9] == 0).all() and torch.isinf(lse[9]).all() and (lse[9] < 0).all()
+        z = lens_list.index(0)
+        assert (out[z] == 0).all() and torch.isinf(lse[z]).all() and (lse[z] < 0).all()
         clean = [torch.nan_to_num(x, nan=0.0) for x in (k, v)]
         check_forward(ext, q, clean[0], clean[1], tk - 1, kv_lens=lens)
 

@@ -11,11 +11,11 @@
 // * work items are (batch*head, chunk of `chunk` keys). A persistent grid of one CTA per SM
 //   takes items dynamically from a counter in the workspace (zeroed by the host before the
 //   launch), so uneven sequence lengths do not unbalance the SMs;
-// * a producer warp streams each item's keys through a STAGES-deep ring of 256-row stages
-//   (32 KiB of K + 32 KiB of V) with 1-D bulk async copies (TMA engine, no multicast,
+// * a producer warp streams each item's keys through a STAGES-deep ring of 384-row stages
+//   (48 KiB of K + 48 KiB of V) with 1-D bulk async copies (TMA engine, no multicast,
 //   evict-first L2 policy), publishing an item header with each stage; rows are read through
 //   the cache strides, so prefix views of a larger cache need no copy;
-// * 8 consumer warps share each stage, one key row per lane: a lane computes the 64-wide dot
+// * 12 consumer warps share each stage, one key row per lane: a lane computes the 64-wide dot
 //   product of its row (16-byte shared reads rotated by lane so 32 rows hit distinct banks; q
 //   is held pre-rotated in registers), the warp takes one max per 32 rows, and for P.V each
 //   lane owns two output features and receives every p by shuffle. Each warp keeps an online
@@ -35,15 +35,15 @@ namespace decode {
 
 constexpr int HD = 64;
 constexpr int ROW_BYTES = HD * 2;                    // 128 B per key row
-constexpr int CONSUMER_WARPS = 8;
+constexpr int CONSUMER_WARPS = 12;
 constexpr int ROWS_PER_WARP = 32;                    // one key row per lane
-constexpr int SUB = CONSUMER_WARPS * ROWS_PER_WARP;  // 256 key rows per ring stage
-constexpr int STAGES = 3;
-constexpr int STAGE_BYTES = 2 * SUB * ROW_BYTES;     // K then V rows: 64 KiB
+constexpr int SUB = CONSUMER_WARPS * ROWS_PER_WARP;  // 384 key rows per ring stage
+constexpr int STAGES = 2;
+constexpr int STAGE_BYTES = 2 * SUB * ROW_BYTES;     // K then V rows: 96 KiB
 constexpr int PRODUCER_WARP = CONSUMER_WARPS;
 constexpr int THREADS = (CONSUMER_WARPS + 1) * 32;
 constexpr int MIN_CHUNK = SUB;
-constexpr int MAX_CHUNK = 1024;                      // keys per work item
+constexpr int MAX_CHUNK = 4 * SUB;                   // 1536 keys per work item
 constexpr int PARTIAL = HD + 4;                      // acc[64], m (log2 units), l, 2 pad:
                                                      // 272 B records keep float4 stores aligned
 constexpr size_t kCounterBytes = 256;                // work counter at the start of the workspace

@@ -59,8 +59,8 @@ bool strides_ok(const int64_t* st) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Keys per decode work item: the largest power of two in [MIN_CHUNK, MAX_CHUNK] that still
-// gives about 8 items per CTA of a persistent grid on a 148-SM part, for load balance (a
+// Keys per decode work item: MAX_CHUNK halved (never below MIN_CHUNK; every value is a multiple
+// of the ring stage) until the shape gives about 8 items per CTA of a persistent grid on a 148-SM part, for load balance (a
 // shape-only heuristic, so the workspace size does not depend on the device).
 int decode_chunk(int64_t bh, int64_t tk) {
   constexpr int64_t kTargetItems = 8 * 148;
