@@ -188,3 +188,34 @@ def test_bf16_native_backward_validation(ext):
         big_lse = lse[:1, :1, :1].expand(shape[:3])
         with pytest.raises(RuntimeError, match=message):
             ext.attention_backward(big, big, big, big, big, big_lse)
+
+
+@torch.no_grad()
+def test_bf16_native_calls_from_a_fresh_thread(ext):
+    """A thread that has made no CUDA runtime call (like autograd's worker) has no current
+    context; the entry points must bind one before encoding their tensor maps."""
+    import threading
+    torch.manual_seed(8)
+    q, k, v = [torch.randn(2, 3, t, 64, device="cuda", dtype=torch.bfloat16) for t in (192, 192, 192)]
+    out, lse = ext.attention_forward(q, k, v)
+    dout = torch.randn_like(out)
+    expected = ext.attention_backward(q, k, v, dout, out, lse)
+    result = {}
+
+    def run():
+        try:
+            result["forward"] = ext.attention_forward(q, k, v)
+            result["backward"] = ext.attention_backward(q, k, v, dout, out, lse)
+            torch.cuda.current_stream().synchronize()
+        except Exception as exc:  # re-raised on the main thread
+            result["error"] = exc
+
+    worker = threading.Thread(target=run)
+    worker.start()
+    worker.join()
+    if "error" in result:
+        raise result["error"]
+    for left, right in zip(result["forward"], (out, lse)):
+        assert torch.equal(left, right)
+    for left, right in zip(result["backward"], expected):
+        assert torch.equal(left, right)

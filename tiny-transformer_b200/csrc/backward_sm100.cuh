@@ -9,22 +9,13 @@
 //   dQ_i  = scale * sum_j bf16(dS_ij) k_j                      (FP32 accumulate, BF16 out)
 // with key j visible to query i iff j <= i + past_len (Tk == Tq + past_len), scale = 1/8.
 //
-// Three kernels, in stream order:
-// * bwd_preprocess_kernel: D, eight lanes per query row (16-byte loads of dO and O).
-// * bwd_dq_kernel: one CTA per (b, h, 128-row query tile), stepping over 64-key tiles.
-//   tcgen05: S = Q.K^T and dP = dO.V^T (SS, M = 128, N = 64, into TMEM); the elementwise warps
-//   (thread = query row = TMEM lane) read them and write bf16 dS over the S columns they have
-//   just read; then dQ += dS.K (TS, A from TMEM). TMEM: S/dS [0,64), dP [64,128), dQ [128,192).
-// * bwd_dkdv_kernel: one CTA per (b, h, 128-key tile), stepping over 64-row query tiles, in
-//   transposed form so that keys are the TMEM lanes: S^T = K.Q^T, dP^T = V.dO^T; the
-//   elementwise warps (thread = key row) write bf16 P^T over S^T and dS^T over dP^T, then
-//   dV += P^T.dO and dK += dS^T.Q (TS). Per-query LSE and D come from shared memory (broadcast
-//   reads). TMEM: S^T/P^T [0,64), dP^T/dS^T [64,128), dV [128,192), dK [192,256).
-// Each step of a CTA is a serial chain (scores -> elementwise -> accumulation). With 256 TMEM
-// columns and ~80 KB of shared memory per CTA, two CTAs share an SM and overlap their chains.
-// Roles: warps 0-3 elementwise + epilogue, warp 4 TMA producer (all lanes stage LSE/D in the
-// dK/dV kernel), warp 5 tcgen05 issuer (one thread). Every mbarrier wait is bounded
-// (TT_ERR_TIMEOUT + abort flag), as in the forward kernels.
+// Three kernels, in stream order (after a memset of the FP32 dQ accumulator):
+// * bwd_preprocess_kernel: -D and -LSE * log2(e) per query row, in rows padded to whole
+//   128-row tiles (eight lanes per row, 16-byte loads of dO and O).
+// * fused::bwd_fused_kernel: one CTA per (b, h, 128-key tile); S, dP and the exponentials are
+//   computed once per (query tile, key tile) pair and feed dV, dK and dQ (see below).
+// * fused::bwd_dq_convert_kernel: dQ = bf16(scale * dQ accumulator).
+// Every mbarrier wait is bounded (TT_ERR_TIMEOUT + abort flag), as in the forward kernels.
 #pragma once
 
 #include <cuda.h>
@@ -36,44 +27,34 @@
 namespace tt {
 namespace backward {
 
-constexpr int TILE = 128;  // rows of the CTA's own tile (UMMA M): query rows or keys
-constexpr int STEP = 64;   // rows of the tile stepped over (UMMA N of the scores)
 constexpr int HD = 64;
-constexpr int STAGES = 3;
-constexpr int THREADS = 192;  // 4 elementwise warps, TMA warp, issuer warp
-constexpr int LOAD_WARP = 4, MMA_WARP = 5;
-constexpr uint32_t TILE_BYTES = TILE * HD * 2;  // 16 KiB
-constexpr uint32_t STEP_BYTES = STEP * HD * 2;  // 8 KiB
-constexpr uint32_t TMEM_COLS = 256;
 constexpr float SCALE = 0.125f;
 constexpr float LOG2E = 1.4426950408889634f;
 
-struct Params {
-  int B, H, Tq, Tk, past_len;
-  int n_tiles;              // query tiles (dQ kernel) or key tiles (dK/dV kernel) of TILE rows
-  const float* lse;         // contiguous [B, H, Tq], natural log
-  const float* D;           // contiguous [B, H, Tq]
-  __nv_bfloat16* out0;      // dQ (dQ kernel) or dK (dK/dV kernel), contiguous
-  __nv_bfloat16* out1;      // dV (dK/dV kernel), contiguous
-};
-
 // ------------------------------------------------------------------ preprocess
 struct PreParams {
-  long long rows;            // B * H * Tq
-  const __nv_bfloat16* dO;   // contiguous [rows, 64]
+  long long rows;            // B * H * Tq_pad (query rows padded to whole 128-row tiles)
+  int Tq, Tq_pad;
+  const __nv_bfloat16* dO;   // contiguous [B * H * Tq, 64]
   const __nv_bfloat16* O;
-  float* D;
+  const float* lse;          // contiguous [B * H * Tq], natural log
+  float* nlse2;              // [B * H * Tq_pad]: -LSE * log2(e), -inf on padding rows
+  float* nd;                 // [B * H * Tq_pad]: -D, 0 on padding rows
 };
 
 // Eight lanes per row, 16-byte loads: a warp covers four rows, a block of 256 threads 32.
 constexpr int PRE_ROWS_PER_BLOCK = 32;
 
 __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const PreParams p) {
-  const long long row =
+  const long long prow =
       static_cast<long long>(blockIdx.x) * PRE_ROWS_PER_BLOCK + (threadIdx.x >> 3);
   const int part = threadIdx.x & 7;  // 8 features per lane
+  const long long bh = prow / p.Tq_pad;
+  const int q = static_cast<int>(prow - bh * p.Tq_pad);
+  const bool real = prow < p.rows && q < p.Tq;
+  const long long row = bh * p.Tq + q;
   float sum = 0.f;
-  if (row < p.rows) {
+  if (real) {
     const uint4 a = reinterpret_cast<const uint4*>(p.dO + row * HD)[part];
     const uint4 o = reinterpret_cast<const uint4*>(p.O + row * HD)[part];
     sum = bf16_lo(a.x) * bf16_lo(o.x) + bf16_hi(a.x) * bf16_hi(o.x) +
@@ -84,41 +65,13 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const PreParams p) 
   // Reduce over the eight lanes of the row (all 32 lanes take part in every shuffle).
 #pragma unroll
   for (int off = 4; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  if (part == 0 && row < p.rows) p.D[row] = sum;
+  if (part == 0 && prow < p.rows) {
+    p.nd[prow] = real ? -sum : 0.f;
+    p.nlse2[prow] = real ? -p.lse[row] * LOG2E : -INFINITY;
+  }
 }
 
 // ------------------------------------------------------------------ shared pieces
-struct alignas(1024) SmemQ {  // dQ kernel
-  uint8_t q[TILE_BYTES];
-  uint8_t dO[TILE_BYTES];
-  uint8_t k[STAGES][STEP_BYTES];
-  uint8_t v[STAGES][STEP_BYTES];
-  uint64_t qd_full;
-  uint64_t kv_full[STAGES], kv_empty[STAGES];
-  uint64_t s_full, s_free, ds_ready, dq_done, drain;
-  uint32_t tmem_base;
-  volatile int abort;
-};
-
-struct alignas(1024) SmemKV {  // dK/dV kernel
-  uint8_t k[TILE_BYTES];
-  uint8_t v[TILE_BYTES];
-  uint8_t q[STAGES][STEP_BYTES];
-  uint8_t dO[STAGES][STEP_BYTES];
-  float lse2[STAGES][STEP];  // LSE * log2(e) per query row of the stage (+inf past Tq)
-  float d[STAGES][STEP];
-  uint64_t kv_full;
-  uint64_t q_full[STAGES], q_empty[STAGES];
-  uint64_t st_full, st_free, pd_ready, acc_done, drain;
-  uint32_t tmem_base;
-  volatile int abort;
-};
-
-constexpr size_t kSmemQ = sizeof(SmemQ) + 1024;
-constexpr size_t kSmemKV = sizeof(SmemKV) + 1024;
-static_assert(2 * kSmemQ <= 228 * 1024 && 2 * kSmemKV <= 228 * 1024,
-              "two CTAs per SM must fit in shared memory");
-
 template <class S>
 __device__ __forceinline__ bool wait_or_abort(S& s, uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
@@ -150,18 +103,6 @@ __device__ __forceinline__ void issue_scores(uint32_t tmem_d, uint32_t a_addr, u
             make_sdesc_sw128(b_addr + kk * 32, 16, 1024), idesc, kk > 0 ? 1u : 0u);
 }
 
-// D += A.B with A = bf16 pairs in TMEM over STEP rows of K, laid out by the elementwise warps
-// as chunk c (K rows [32c, 32c + 32)) at TMEM columns [32c, 32c + 16) of its region; B = a
-// STEP x 64 tile, MN-major (16 K rows x 128 B = 2048 B per k-step).
-__device__ __forceinline__ void issue_accumulate(uint32_t tmem_d, uint32_t tmem_a, uint32_t b_addr,
-                                                 uint32_t idesc, bool accumulate) {
-#pragma unroll
-  for (int kk = 0; kk < STEP / 16; ++kk)
-    umma_ts(tmem_d, tmem_a + 32 * (kk >> 1) + 8 * (kk & 1),
-            make_sdesc_sw128(b_addr + kk * 2048, 8192, 1024), idesc,
-            (accumulate || kk > 0) ? 1u : 0u);
-}
-
 __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_t (&acc)[32],
                                                float scale) {
   uint32_t packed[16];
@@ -175,183 +116,160 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_
     d4[e] = make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
 }
 
-// ------------------------------------------------------------------ dQ kernel
-__global__ void __launch_bounds__(THREADS, 2)
-bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-              const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  SmemQ& s = *reinterpret_cast<SmemQ*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                       ~uintptr_t(1023));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BH = p.B * p.H;
-  const int qt = p.n_tiles - 1 - static_cast<int>(blockIdx.x / BH);  // heaviest tiles first
-  const int bh = static_cast<int>(blockIdx.x % BH);
-  const int b = bh / p.H, h = bh % p.H;
-  const int q0 = qt * TILE;
-  const long long kend =
-      min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + TILE + p.past_len);
-  const int n_kv = static_cast<int>((kend + STEP - 1) / STEP);  // key steps this tile sees
-  constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128;
+// ------------------------------------------------------------------ fused dQ/dK/dV kernel
+// One CTA per (b, h, 128-key tile), stepping over 128-row query tiles in transposed form (keys
+// are the TMEM lanes). Per step, all products are M = 128 tcgen05 MMAs:
+//   S^T = K.Q^T, dP^T = V.dO^T        (SS, N = 128)
+//   dV += P^T.dO                      (TS, A = bf16 P^T in its own TMEM columns)
+//   dK += dS^T.Q                      (TS, A = bf16 dS^T written over dP^T)
+//   dQ_step = dS.K                    (SS, A = dS staged in shared memory, MN-major)
+// dQ_step is read out of TMEM by four drain warps and added into an FP32 dQ workspace with TMA
+// bulk reduce-add (one 32 x 32 box per warp and feature half); bwd_dq_convert_kernel scales it
+// and rounds it to bf16 afterwards. S, dP and the exponentials are computed once per pair of
+// tiles, and every score product has N = 128.
+//
+// The elementwise warps work in two phases per step: (1) load S^T, release it, compute
+// P = exp2(S * scale * log2(e) - LSE * log2(e)) and store bf16 P^T; (2) load dP^T, compute
+// dS = P * (dP - D) from the FP32 P kept in registers, store bf16 dS^T over dP^T and dS into
+// shared memory. Two issuer threads feed the tensor core (a tcgen05.mma blocks its thread for
+// about its execution time, so one thread would delay each product behind the others):
+//   scores issuer:     S^T(i+1) once S^T(i) is released (overlapping both phases of step i);
+//                      dP^T(i+1) once dK(i) has completed (it overwrites dS^T(i));
+//   accumulate issuer: dV(i) once P^T(i) is stored; dK(i), then dQ(i), once dS(i) is stored;
+// so phase 1 of step i+1 starts as soon as phase 2 of step i ends. (Measured on cfg3 against
+// other assignments: S and dV on one thread with dK, dP, dQ on the other, 5 % slower; three
+// issuer warps, 2-5 % slower.)
+// TMEM: S^T [0,128), dP^T/dS^T [128,256), dV [256,320), dK [320,384), dQ [384,448),
+// P^T [448,512) of 512 columns.
+// Roles: warps 0-7 elementwise (warp w: TMEM lanes 32 (w % 4) .., query columns 64 (w / 4) ..),
+// warps 8-11 dQ drain (lanes 32 (w % 4) ..), warp 12 TMA producer, warp 13 accumulate issuer
+// (and TMEM owner), warp 14 scores issuer.
+namespace fused {
 
-  if (threadIdx.x == 0) {
-    mbar_init(&s.qd_full, 1);
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&s.kv_full[i], 1);
-      mbar_init(&s.kv_empty[i], 1);
-    }
-    mbar_init(&s.s_full, 1);
-    mbar_init(&s.s_free, 4);
-    mbar_init(&s.ds_ready, 4);
-    mbar_init(&s.dq_done, 1);
-    mbar_init(&s.drain, 1);
-    s.abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == MMA_WARP) {
-    tmem_alloc(&s.tmem_base, TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = s.tmem_base;
+constexpr int T = 128;          // keys per CTA tile and query rows per step
+constexpr int STAGES = 3;       // Q / dO / LSE / D ring
+constexpr int EW_WARPS = 8, DQ_WARP0 = 8, LOAD_WARP = 12, MMA_WARP = 13, SCORE_WARP = 14;
+constexpr int THREADS = 15 * 32;
+constexpr uint32_t TILE_BYTES = T * HD * 2;  // 16 KiB
+constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384, T_P = 448;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int DQ_BOX_ROWS = 32;  // dQ reduce box: 32 rows x 32 FP32 features (128 B, SW128)
 
-  if (warp == LOAD_WARP) {
-    if (lane == 0) {
-      int issued = 0;
-      mbar_arrive_expect_tx(&s.qd_full, 2 * TILE_BYTES);
-      tma_load_4d(s.q, &tm_q, &s.qd_full, 0, q0, h, b);
-      tma_load_4d(s.dO, &tm_do, &s.qd_full, 0, q0, h, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % STAGES;
-        if (j >= STAGES && !wait_or_abort(s, &s.kv_empty[st], ((j / STAGES) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&s.kv_full[st], 2 * STEP_BYTES);
-        tma_load_4d(s.k[st], &tm_k, &s.kv_full[st], 0, j * STEP, h, b);
-        tma_load_4d(s.v[st], &tm_v, &s.kv_full[st], 0, j * STEP, h, b);
-        issued = j + 1;
-      }
-      if (s.abort) {
-        mbar_wait(&s.qd_full, 0);
-        for (int j = max(0, issued - STAGES); j < issued; ++j)
-          mbar_wait(&s.kv_full[j % STAGES], (j / STAGES) & 1);
-      }
-    }
-  } else if (warp == MMA_WARP) {
-    if (lane == 0) {
-      const uint32_t idesc_s = make_idesc_bf16(TILE, STEP, false);
-      const uint32_t idesc_o = make_idesc_bf16(TILE, HD, true);
-      const uint32_t q_addr = smem_u32(s.q), do_addr = smem_u32(s.dO);
-      bool ok = wait_or_abort(s, &s.qd_full, 0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % STAGES;
-        if (!wait_or_abort(s, &s.kv_full[st], (j / STAGES) & 1)) break;
-        if (j > 0 && !wait_or_abort(s, &s.s_free, (j - 1) & 1)) break;
-        tc_fence_after();
-        issue_scores(tmem + T_S, q_addr, smem_u32(s.k[st]), idesc_s);
-        issue_scores(tmem + T_DP, do_addr, smem_u32(s.v[st]), idesc_s);
-        umma_commit(&s.s_full);
-        if (!wait_or_abort(s, &s.ds_ready, j & 1)) break;
-        tc_fence_after();
-        issue_accumulate(tmem + T_DQ, tmem + T_S, smem_u32(s.k[st]), idesc_o, j > 0);
-        umma_commit(&s.dq_done);
-        umma_commit(&s.kv_empty[st]);
-      }
-      // All MMAs issued by this thread have completed once `drain` flips.
-      umma_commit(&s.drain);
-      mbar_wait(&s.drain, 0);
-    }
-  } else {
-    // Elementwise warps: thread = query row r of the tile = TMEM lane.
-    const int wq = warp, r = wq * 32 + lane;
-    const int row = q0 + r;
-    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const size_t ridx = static_cast<size_t>(bh) * p.Tq + static_cast<size_t>(row);
-    const float lse2 = row < p.Tq ? p.lse[ridx] * LOG2E : INFINITY;
-    const float drow = row < p.Tq ? p.D[ridx] : 0.f;
-    const long long row_limit = static_cast<long long>(row) + p.past_len;
-    const long long tile_limit = static_cast<long long>(q0) + p.past_len;
-    const float sl2 = SCALE * LOG2E;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait(s, &s.s_full, j & 1)) { ok = false; break; }
-      // dS overwrites S, which the previous dQ += dS.K may still be reading.
-      if (j > 0 && !warp_wait(s, &s.dq_done, (j - 1) & 1)) { ok = false; break; }
-      tc_fence_after();
-      const long long kv0 = static_cast<long long>(j) * STEP;
-      const bool masked = kv0 + STEP - 1 > tile_limit;
-#pragma unroll
-      for (int c = 0; c < STEP / 32; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + T_S + c * 32, sr);
-        tmem_ld32(tmem + lane_base + T_DP + c * 32, dr);
-        tmem_wait_ld();
-        reg_fence(sr);
-        reg_fence(dr);
-        uint32_t ds[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = 2 * e + u;
-            float pp = ex2_approx(__uint_as_float(sr[col]) * sl2 - lse2);
-            if (masked && kv0 + c * 32 + col > row_limit) pp = 0.f;
-            dv[u] = pp * (__uint_as_float(dr[col]) - drow);
-          }
-          ds[e] = pack_bf16x2(dv[0], dv[1]);
-        }
-        tmem_st16(tmem + lane_base + T_S + c * 32, ds);  // over S columns this thread has read
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s.s_free);
-        mbar_arrive(&s.ds_ready);
-      }
-    }
-    if (ok && warp_wait(s, &s.dq_done, (n_kv - 1) & 1)) {
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t acc[32];
-        tmem_ld32(tmem + lane_base + T_DQ + c * 32, acc);
-        tmem_wait_ld();
-        reg_fence(acc);
-        if (row < p.Tq) store_row_bf16(p.out0 + ridx * HD + c * 32, acc, SCALE);
-      }
-    }
-  }
+struct Params {
+  int B, H, Tq, Tk, past_len;
+  int n_k_tiles;
+  int Tq_pad;           // Tq rounded up to whole 128-row tiles
+  const float* nlse2;   // [B, H, Tq_pad]: -LSE * log2(e), -inf on padding rows
+  const float* nd;      // [B, H, Tq_pad]: -D
+  __nv_bfloat16* dk;    // contiguous [B, H, Tk, 64]
+  __nv_bfloat16* dv;
+};
 
-  tc_fence_before();
-  __syncthreads();
-  if (warp == MMA_WARP) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+struct alignas(1024) Smem {
+  uint8_t k[TILE_BYTES];
+  uint8_t v[TILE_BYTES];
+  uint8_t q[STAGES][TILE_BYTES];
+  uint8_t dO[STAGES][TILE_BYTES];
+  // dS of the step as the MN-major A operand of dQ = dS.K: atom column c (queries [64c, 64c+64))
+  // holds one 128-byte row per key (K index), 16-byte chunks XOR-swizzled by key & 7.
+  uint8_t ds[2][T * 128];
+  // Per drain warp, the two feature halves of its 32 dQ rows, 128-byte swizzled.
+  uint8_t dq_stage[4][2][DQ_BOX_ROWS * 128];
+  float nlse2[STAGES][T];  // -LSE * log2(e) per query row of the stage (-inf past Tq)
+  float nd[STAGES][T];     // -D per query row of the stage
+  uint64_t kv_full;
+  uint64_t q_full[STAGES], q_empty[STAGES];
+  uint64_t s_full, s_consumed, p_full, pv_free, dp_full, ds_ready, ds_free, dk_done;
+  uint64_t dq_full, dq_free, acc_final, drain, drain_scores;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "fused backward shared memory");
+
+// dQ_step = dS.K: A = dS (MN-major, two 64-query atom columns 16 KiB apart), B = K tile
+// (MN-major over features), K = 128 keys in 8 steps of 16 key rows (2048 B in both operands).
+__device__ __forceinline__ void issue_dq(uint32_t tmem_d, uint32_t ds_addr, uint32_t k_addr,
+                                         uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < T / 16; ++kk)
+    umma_ss(tmem_d, make_sdesc_sw128(ds_addr + kk * 2048, T * 128, 1024),
+            make_sdesc_sw128(k_addr + kk * 2048, 8192, 1024), idesc, kk > 0 ? 1u : 0u);
+}
+
+// D += A.B, K = 128 rows in 8 steps of 16, B = a 128 x 64 MN-major tile (2048 B per step).
+// A = bf16 pairs in TMEM: DENSE, 8 columns per step from tmem_a; otherwise chunk c of 32 K rows
+// at columns [32c, 32c + 16) (the layout written over a 128-column FP32 region).
+template <bool DENSE>
+__device__ __forceinline__ void issue_accumulate128(uint32_t tmem_d, uint32_t tmem_a,
+                                                    uint32_t b_addr, uint32_t idesc,
+                                                    bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < T / 16; ++kk)
+    umma_ts(tmem_d, tmem_a + (DENSE ? 8 * kk : 32 * (kk >> 1) + 8 * (kk & 1)),
+            make_sdesc_sw128(b_addr + kk * 2048, 8192, 1024), idesc,
+            (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// Phase 1 for one 32-query chunk: p = exp2(S * scale * log2(e) - LSE * log2(e)), packed to bf16
+// pairs; with MASKED, queries before chunk column `first_visible` get p = 0.
+template <bool MASKED>
+__device__ __forceinline__ void ew_probs(const uint32_t (&sr)[32], uint32_t nlse_addr,
+                                         int first_visible, float* p, uint32_t (&pk)[16]) {
+  const uint64_t sc2 = f2_pack(SCALE * LOG2E, SCALE * LOG2E);
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const float4 nl = lds_f4(nlse_addr + 16 * g);
+    float x[4];
+    f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[4 * g]), __uint_as_float(sr[4 * g + 1])), sc2,
+                     f2_pack(nl.x, nl.y)), x[0], x[1]);
+    f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[4 * g + 2]), __uint_as_float(sr[4 * g + 3])), sc2,
+                     f2_pack(nl.z, nl.w)), x[2], x[3]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      p[4 * g + u] = ex2_approx(x[u]);
+      if (MASKED && 4 * g + u < first_visible) p[4 * g + u] = 0.f;
+    }
+    pk[2 * g] = pack_bf16x2(p[4 * g], p[4 * g + 1]);
+    pk[2 * g + 1] = pack_bf16x2(p[4 * g + 2], p[4 * g + 3]);
   }
 }
 
-// ------------------------------------------------------------------ dK/dV kernel
-__global__ void __launch_bounds__(THREADS, 2)
-bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                const Params p) {
+// Phase 2 for 16 queries: ds = p * (dP - D), packed to bf16 pairs (p: the 16 FP32
+// probabilities of these queries).
+__device__ __forceinline__ void ew_dscores(const float* p, const uint32_t (&dr)[16],
+                                           uint32_t nd_addr, uint32_t (&dsb)[8]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float4 nd = lds_f4(nd_addr + 16 * g);
+    const uint64_t d01 = f2_add(
+        f2_pack(__uint_as_float(dr[4 * g]), __uint_as_float(dr[4 * g + 1])), f2_pack(nd.x, nd.y));
+    const uint64_t d23 = f2_add(
+        f2_pack(__uint_as_float(dr[4 * g + 2]), __uint_as_float(dr[4 * g + 3])), f2_pack(nd.z, nd.w));
+    float ds[4];
+    f2_unpack(f2_mul(f2_pack(p[4 * g], p[4 * g + 1]), d01), ds[0], ds[1]);
+    f2_unpack(f2_mul(f2_pack(p[4 * g + 2], p[4 * g + 3]), d23), ds[2], ds[3]);
+    dsb[2 * g] = pack_bf16x2(ds[0], ds[1]);
+    dsb[2 * g + 1] = pack_bf16x2(ds[2], ds[3]);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                 const __grid_constant__ CUtensorMap tm_dqacc, const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  SmemKV& s = *reinterpret_cast<SmemKV*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                         ~uintptr_t(1023));
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int BH = p.B * p.H;
   const int kt = static_cast<int>(blockIdx.x / BH);  // low key tiles see the most queries
   const int bh = static_cast<int>(blockIdx.x % BH);
   const int b = bh / p.H, h = bh % p.H;
-  const int k0 = kt * TILE;
-  // Query steps (of STEP rows) that see some key of this tile: from the step holding query
-  // k0 - past_len on; the last query row sees every key, so there is at least one.
-  const int qs0 = static_cast<int>(max(0LL, static_cast<long long>(k0) - p.past_len) / STEP);
-  const int n_q = (p.Tq + STEP - 1) / STEP - qs0;
-  constexpr uint32_t T_ST = 0, T_DPT = 64, T_DV = 128, T_DK = 192;
+  const int k0 = kt * T;
+  // Query tiles that see some key of this tile: from the one holding query k0 - past_len on.
+  const int qt0 = static_cast<int>(max(0LL, static_cast<long long>(k0) - p.past_len) / T);
+  const int n_q = (p.Tq + T - 1) / T - qt0;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.kv_full, 1);
@@ -359,11 +277,19 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       mbar_init(&s.q_full[i], 1);
       mbar_init(&s.q_empty[i], 1);
     }
-    mbar_init(&s.st_full, 1);
-    mbar_init(&s.st_free, 4);
-    mbar_init(&s.pd_ready, 4);
-    mbar_init(&s.acc_done, 1);
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.s_consumed, EW_WARPS);
+    mbar_init(&s.p_full, EW_WARPS);
+    mbar_init(&s.pv_free, 1);
+    mbar_init(&s.dp_full, 1);
+    mbar_init(&s.ds_ready, EW_WARPS);
+    mbar_init(&s.ds_free, 1);
+    mbar_init(&s.dk_done, 1);
+    mbar_init(&s.dq_full, 1);
+    mbar_init(&s.dq_free, 4);
+    mbar_init(&s.acc_final, 1);
     mbar_init(&s.drain, 1);
+    mbar_init(&s.drain_scores, 1);
     s.abort = 0;
     fence_barrier_init();
   }
@@ -385,23 +311,15 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     }
     for (int i = 0; i < n_q; ++i) {
       const int st = i % STAGES;
-      const int q0 = (qs0 + i) * STEP;
+      const int q0 = (qt0 + i) * T;
       if (i >= STAGES && !warp_wait(s, &s.q_empty[st], ((i / STAGES) - 1) & 1)) break;
-      // Per-query LSE (log2 units) and D of this step; rows past Tq get +inf / 0, so their
-      // probabilities are exactly zero.
-#pragma unroll
-      for (int e = 0; e < STEP / 32; ++e) {
-        const int rr = e * 32 + lane;
-        const int q = q0 + rr;
-        const size_t idx = static_cast<size_t>(bh) * p.Tq + static_cast<size_t>(q);
-        s.lse2[st][rr] = q < p.Tq ? p.lse[idx] * LOG2E : INFINITY;
-        s.d[st][rr] = q < p.Tq ? p.D[idx] : 0.f;
-      }
-      __syncwarp();
       if (lane == 0) {
-        mbar_arrive_expect_tx(&s.q_full[st], 2 * STEP_BYTES);
+        const size_t row = static_cast<size_t>(bh) * p.Tq_pad + static_cast<size_t>(q0);
+        mbar_arrive_expect_tx(&s.q_full[st], 2 * TILE_BYTES + 2 * T * sizeof(float));
         tma_load_4d(s.q[st], &tm_q, &s.q_full[st], 0, q0, h, b);
         tma_load_4d(s.dO[st], &tm_do, &s.q_full[st], 0, q0, h, b);
+        bulk_load_plain(s.nlse2[st], p.nlse2 + row, T * sizeof(float), &s.q_full[st]);
+        bulk_load_plain(s.nd[st], p.nd + row, T * sizeof(float), &s.q_full[st]);
       }
       issued = i + 1;
     }
@@ -410,95 +328,199 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       for (int i = max(0, issued - STAGES); i < issued; ++i)
         mbar_wait(&s.q_full[i % STAGES], (i / STAGES) & 1);
     }
+  } else if (warp == SCORE_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc_bf16(T, T, false);
+      const uint32_t k_addr = smem_u32(s.k), v_addr = smem_u32(s.v);
+      bool ok = wait_or_abort(s, &s.kv_full, 0) && wait_or_abort(s, &s.q_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        issue_scores(tmem + T_ST, k_addr, smem_u32(s.q[0]), idesc_s);
+        umma_commit(&s.s_full);
+        issue_scores(tmem + T_DPT, v_addr, smem_u32(s.dO[0]), idesc_s);
+        umma_commit(&s.dp_full);
+      }
+      for (int i = 0; ok && i + 1 < n_q; ++i) {
+        const int sn = (i + 1) % STAGES;
+        if (!wait_or_abort(s, &s.q_full[sn], ((i + 1) / STAGES) & 1)) break;
+        // S^T(i+1) as soon as the elementwise warps hold S^T(i) in registers.
+        if (!wait_or_abort(s, &s.s_consumed, i & 1)) break;
+        tc_fence_after();
+        issue_scores(tmem + T_ST, k_addr, smem_u32(s.q[sn]), idesc_s);
+        umma_commit(&s.s_full);
+        // dP^T(i+1) overwrites dS^T(i): after dK(i) has completed.
+        if (!wait_or_abort(s, &s.dk_done, i & 1)) break;
+        tc_fence_after();
+        issue_scores(tmem + T_DPT, v_addr, smem_u32(s.dO[sn]), idesc_s);
+        umma_commit(&s.dp_full);
+      }
+      umma_commit(&s.drain_scores);
+      mbar_wait(&s.drain_scores, 0);
+    }
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
-      const uint32_t idesc_s = make_idesc_bf16(TILE, STEP, false);
-      const uint32_t idesc_o = make_idesc_bf16(TILE, HD, true);
-      const uint32_t k_addr = smem_u32(s.k), v_addr = smem_u32(s.v);
-      bool ok = wait_or_abort(s, &s.kv_full, 0);
-      for (int i = 0; ok && i < n_q; ++i) {
+      const uint32_t idesc_o = make_idesc_bf16(T, HD, true);
+      const uint32_t idesc_dq = make_idesc_bf16(T, HD, true) | (1u << 15);  // A MN-major
+      const uint32_t k_addr = smem_u32(s.k);
+      for (int i = 0; i < n_q; ++i) {
         const int st = i % STAGES;
-        if (!wait_or_abort(s, &s.q_full[st], (i / STAGES) & 1)) break;
-        if (i > 0 && !wait_or_abort(s, &s.st_free, (i - 1) & 1)) break;
+        if (!wait_or_abort(s, &s.p_full, i & 1)) break;
         tc_fence_after();
-        issue_scores(tmem + T_ST, k_addr, smem_u32(s.q[st]), idesc_s);
-        issue_scores(tmem + T_DPT, v_addr, smem_u32(s.dO[st]), idesc_s);
-        umma_commit(&s.st_full);
-        if (!wait_or_abort(s, &s.pd_ready, i & 1)) break;
+        issue_accumulate128<true>(tmem + T_DV, tmem + T_P, smem_u32(s.dO[st]), idesc_o, i > 0);
+        umma_commit(&s.pv_free);
+        if (!wait_or_abort(s, &s.ds_ready, i & 1)) break;
         tc_fence_after();
-        issue_accumulate(tmem + T_DV, tmem + T_ST, smem_u32(s.dO[st]), idesc_o, i > 0);
-        issue_accumulate(tmem + T_DK, tmem + T_DPT, smem_u32(s.q[st]), idesc_o, i > 0);
-        umma_commit(&s.acc_done);
+        issue_accumulate128<false>(tmem + T_DK, tmem + T_DPT, smem_u32(s.q[st]), idesc_o, i > 0);
+        umma_commit(&s.dk_done);
+        // Q(i) and dO(i) were last read by dV(i) and dK(i); S^T(i) and dP^T(i) (scores
+        // issuer) completed before the elementwise warps could read them.
         umma_commit(&s.q_empty[st]);
+        if (i + 1 == n_q) umma_commit(&s.acc_final);
+        if (i > 0 && !wait_or_abort(s, &s.dq_free, (i - 1) & 1)) break;
+        tc_fence_after();
+        issue_dq(tmem + T_DQ, smem_u32(s.ds[0]), k_addr, idesc_dq);
+        umma_commit(&s.dq_full);
+        umma_commit(&s.ds_free);
       }
+      // All MMAs issued by this thread have completed once `drain` flips.
       umma_commit(&s.drain);
       mbar_wait(&s.drain, 0);
     }
+  } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + 4) {
+    // dQ drain: thread = query row 32 * quarter + lane of the step = TMEM lane.
+    const int quarter = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t* box0 = s.dq_stage[quarter][0];
+    uint8_t* box1 = s.dq_stage[quarter][1];
+    for (int i = 0; i < n_q; ++i) {
+      if (!warp_wait(s, &s.dq_full, i & 1)) break;
+      tc_fence_after();
+      uint32_t a0[32], a1[32];
+      tmem_ld32(tmem + lane_base + T_DQ, a0);
+      tmem_ld32(tmem + lane_base + T_DQ + 32, a1);
+      tmem_wait_ld();
+      reg_fence(a0);
+      reg_fence(a1);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.dq_free);
+        bulk_wait_group_read_all();  // the previous step's reduce has read the staging boxes
+      }
+      __syncwarp();
+      const uint32_t sw = lane & 7;
+      const uint32_t row0_addr = smem_u32(box0) + lane * 128;
+      const uint32_t row1_addr = smem_u32(box1) + lane * 128;
+#pragma unroll
+      for (uint32_t j = 0; j < 8; ++j) {
+        sts_u4(row0_addr + ((j ^ sw) << 4), a0[4 * j], a0[4 * j + 1], a0[4 * j + 2], a0[4 * j + 3]);
+        sts_u4(row1_addr + ((j ^ sw) << 4), a1[4 * j], a1[4 * j + 1], a1[4 * j + 2], a1[4 * j + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      const int row0 = (qt0 + i) * T + quarter * DQ_BOX_ROWS;
+      if (lane == 0 && row0 < p.Tq) {  // rows past Tq inside a box are clipped by the map
+        tma_reduce_add_4d(box0, &tm_dqacc, 0, row0, h, b);
+        tma_reduce_add_4d(box1, &tm_dqacc, 32, row0, h, b);
+        bulk_commit_group();
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();
   } else {
-    // Elementwise warps: thread = key row of the tile = TMEM lane.
-    const int wq = warp, r = wq * 32 + lane;
+    // Elementwise warps: thread = key row of the tile = TMEM lane; this warp covers query
+    // columns [64 * half, 64 * half + 64) of each step, as two chunks of 32.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
     const int key = k0 + r;
-    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const float sl2 = SCALE * LOG2E;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + T_ST + half * 64;
+    const uint32_t t_dp = tmem + lane_base + T_DPT + half * 64;
+    const uint32_t t_p = tmem + lane_base + T_P + half * 32;
+    const uint32_t ds_row = smem_u32(s.ds[half]) + r * 128;
+    const uint32_t sw = static_cast<uint32_t>(r & 7);
     bool ok = true;
     for (int i = 0; i < n_q; ++i) {
       const int st = i % STAGES;
-      const long long q0 = static_cast<long long>(qs0 + i) * STEP;
-      if (!warp_wait(s, &s.st_full, i & 1)) { ok = false; break; }
-      // P^T / dS^T overwrite S^T / dP^T, which the previous accumulation may still read.
-      if (i > 0 && !warp_wait(s, &s.acc_done, (i - 1) & 1)) { ok = false; break; }
+      const long long q0 = static_cast<long long>(qt0 + i) * T;
+      const uint32_t nl_addr = smem_u32(&s.nlse2[st][half * 64]);
+      const uint32_t nd_addr = smem_u32(&s.nd[st][half * 64]);
+      // Pair (key, q) is visible iff q >= key - past_len; only steps crossing the diagonal mask.
+      const bool masked = static_cast<long long>(k0) + T - 1 > q0 + p.past_len;
+      const int first_visible = static_cast<int>(min(static_cast<long long>(T),
+          max(0LL, key - p.past_len - q0))) - half * 64;  // column of this warp's 64
+
+      // Phase 1: P from S^T.
+      if (!warp_wait(s, &s.s_full, i & 1)) { ok = false; break; }
       tc_fence_after();
-      // Pair (key, q) is visible iff key <= q + past_len; only steps crossing the diagonal mask.
-      const bool masked = static_cast<long long>(k0) + TILE - 1 > q0 + p.past_len;
-#pragma unroll
-      for (int c = 0; c < STEP / 32; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + T_ST + c * 32, sr);
-        tmem_ld32(tmem + lane_base + T_DPT + c * 32, dr);
+      float pr[64];
+      {
+        uint32_t sr0[32], sr1[32];
+        tmem_ld32(t_s, sr0);
+        tmem_ld32(t_s + 32, sr1);
         tmem_wait_ld();
-        reg_fence(sr);
-        reg_fence(dr);
-        uint32_t pk[16], ds[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = 2 * e + u;
-            const int qc = c * 32 + col;
-            float pp = ex2_approx(__uint_as_float(sr[col]) * sl2 - s.lse2[st][qc]);
-            if (masked && static_cast<long long>(key) > q0 + qc + p.past_len) pp = 0.f;
-            pv[u] = pp;
-            dv[u] = pp * (__uint_as_float(dr[col]) - s.d[st][qc]);
-          }
-          pk[e] = pack_bf16x2(pv[0], pv[1]);
-          ds[e] = pack_bf16x2(dv[0], dv[1]);
-        }
-        tmem_st16(tmem + lane_base + T_ST + c * 32, pk);   // over S^T columns just read
-        tmem_st16(tmem + lane_base + T_DPT + c * 32, ds);  // over dP^T columns just read
+        reg_fence(sr0);
+        reg_fence(sr1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.s_consumed);
+        // P^T(i - 1) has been read by dV(i - 1) (long done by now, normally).
+        if (i > 0 && !warp_wait(s, &s.pv_free, (i - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t pk[16];
+        if (masked) ew_probs<true>(sr0, nl_addr, first_visible, pr, pk);
+        else ew_probs<false>(sr0, nl_addr, 0, pr, pk);
+        tmem_st16(t_p, pk);
+        if (masked) ew_probs<true>(sr1, nl_addr + 128, first_visible - 32, pr + 32, pk);
+        else ew_probs<false>(sr1, nl_addr + 128, 0, pr + 32, pk);
+        tmem_st16(t_p + 16, pk);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s.st_free);
-        mbar_arrive(&s.pd_ready);
-      }
-    }
-    if (ok && warp_wait(s, &s.acc_done, (n_q - 1) & 1)) {
+      if (lane == 0) mbar_arrive(&s.p_full);
+
+      // Phase 2: dS from dP^T and the FP32 P, 16 queries at a time.
+      if (!warp_wait(s, &s.dp_full, i & 1)) { ok = false; break; }
       tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t dr[16], dsb[8];
+        tmem_ld16(t_dp + 16 * c, dr);
+        tmem_wait_ld();
+        reg_fence16(dr);
+        ew_dscores(pr + 16 * c, dr, nd_addr + 64 * c, dsb);
+        // over dP^T columns just read: 32-query chunk 2 * half + c / 2, 8 columns per 16 queries
+        tmem_st8(tmem + lane_base + T_DPT + 32 * (2 * half + (c >> 1)) + 8 * (c & 1), dsb);
+        // The dS tile was last read by dQ(i - 1).
+        if (c == 0 && i > 0 && !warp_wait(s, &s.ds_free, (i - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        const uint32_t j = 2 * c;  // 8-query chunks j, j + 1 of the half
+        sts_u4(ds_row + ((j ^ sw) << 4), dsb[0], dsb[1], dsb[2], dsb[3]);
+        sts_u4(ds_row + (((j + 1) ^ sw) << 4), dsb[4], dsb[5], dsb[6], dsb[7]);
+      }
+      if (!ok) break;
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.ds_ready);
+    }
+    if (ok && warp_wait(s, &s.acc_final, 0)) {
+      tc_fence_after();
+      // Warps 0-3 write dK, warps 4-7 dV (same TMEM lanes, different columns).
       const size_t kidx = static_cast<size_t>(bh) * p.Tk + static_cast<size_t>(key);
+      const uint32_t col = half == 0 ? T_DK : T_DV;
+      __nv_bfloat16* out = half == 0 ? p.dk : p.dv;
+      const float scale = half == 0 ? SCALE : 1.f;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t acc[32];
-        tmem_ld32(tmem + lane_base + T_DK + c * 32, acc);
+        tmem_ld32(tmem + lane_base + col + c * 32, acc);
         tmem_wait_ld();
         reg_fence(acc);
-        if (key < p.Tk) store_row_bf16(p.out0 + kidx * HD + c * 32, acc, SCALE);
-        tmem_ld32(tmem + lane_base + T_DV + c * 32, acc);
-        tmem_wait_ld();
-        reg_fence(acc);
-        if (key < p.Tk) store_row_bf16(p.out1 + kidx * HD + c * 32, acc, 1.f);
+        if (key < p.Tk) store_row_bf16(out + kidx * HD + c * 32, acc, scale);
       }
     }
   }
@@ -511,6 +533,25 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     tmem_dealloc(tmem, TMEM_COLS);
   }
 }
+
+// dQ = bf16(scale * dQ_acc), eight features per thread.
+struct ConvertParams {
+  long long rows;       // B * H * Tq
+  const float* acc;     // [rows, 64]
+  __nv_bfloat16* dq;    // [rows, 64]
+};
+
+__global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const ConvertParams p) {
+  const long long i = static_cast<long long>(blockIdx.x) * 256 + threadIdx.x;  // 8-feature group
+  if (i >= p.rows * (HD / 8)) return;
+  const float4 a = reinterpret_cast<const float4*>(p.acc)[2 * i];
+  const float4 c = reinterpret_cast<const float4*>(p.acc)[2 * i + 1];
+  reinterpret_cast<uint4*>(p.dq)[i] =
+      make_uint4(pack_bf16x2(a.x * SCALE, a.y * SCALE), pack_bf16x2(a.z * SCALE, a.w * SCALE),
+                 pack_bf16x2(c.x * SCALE, c.y * SCALE), pack_bf16x2(c.z * SCALE, c.w * SCALE));
+}
+
+}  // namespace fused
 
 }  // namespace backward
 }  // namespace tt

@@ -60,8 +60,9 @@ bool strides_ok(const int64_t* st) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Keys per decode work item: MAX_CHUNK halved (never below MIN_CHUNK; every value is a multiple
-// of the ring stage) until the shape gives about 8 items per CTA of a persistent grid on a 148-SM part, for load balance (a
-// shape-only heuristic, so the workspace size does not depend on the device).
+// of the ring stage) until the shape gives about 8 items per CTA of a persistent grid on a
+// 148-SM part, for load balance (a shape-only heuristic, so the workspace size does not depend
+// on the device).
 int decode_chunk(int64_t bh, int64_t tk) {
   constexpr int64_t kTargetItems = 8 * 148;
   int chunk = tt::decode::MAX_CHUNK;
@@ -119,6 +120,34 @@ bool encode_map(CUtensorMap* map, const void* base, const Shape4& s, std::string
   return true;
 }
 
+// FP32 [B, H, T, 64] map for the backward's dQ accumulator: boxes of 32 features (128 bytes,
+// 128-byte swizzle) x box_rows rows, written by bulk tensor reduce-add.
+bool encode_map_f32(CUtensorMap* map, void* base, const Shape4& s, std::string* err,
+                    unsigned box_rows) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
+    return false;
+  }
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(s.size[3]), static_cast<cuuint64_t>(s.size[2]),
+                              static_cast<cuuint64_t>(s.size[1]), static_cast<cuuint64_t>(s.size[0])};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(s.stride[2]) * 4,
+                                 static_cast<cuuint64_t>(s.stride[1]) * 4,
+                                 static_cast<cuuint64_t>(s.stride[0]) * 4};
+  const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(box_rows), 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    *err = buf;
+    return false;
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ per-device setup
 struct DeviceState {
   bool checked = false;
@@ -134,6 +163,11 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(TT_ATTN_UNSUPPORTED, "device index out of range");
+  // Make the device's primary context current on this thread: a thread that has made no
+  // runtime call yet (e.g. an autograd worker) has none, and the driver-API tensor-map
+  // encoding that follows needs one.
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
   *dev_out = dev;
   std::lock_guard<std::mutex> lock(g_dev_mu);
   DeviceState& ds = g_dev[dev];
@@ -188,13 +222,9 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tt::decode::kSmemBytes));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tt::backward::bwd_dq_kernel,
+      e = cudaFuncSetAttribute(tt::backward::fused::bwd_fused_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(tt::backward::kSmemQ));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(tt::backward::bwd_dkdv_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(tt::backward::kSmemKV));
+                               static_cast<int>(tt::backward::fused::kSmemBytes));
     if (e != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     ds.attrs_set = true;
@@ -323,10 +353,20 @@ TT_ATTN_API tt_attn_status tt_rope_append_bf16(
   return check_launch("rope_append_kernel launch");
 }
 
+// Backward workspace: -LSE * log2(e) and -D per query row, each [B, H, Tq_pad] FP32 with Tq
+// padded to whole 128-row tiles (so every tile's rows are one aligned 512-byte copy), then the
+// FP32 dQ accumulator [B, H, Tq, 64] that the fused kernel reduces into.
+int64_t backward_q_pad(int64_t q_len) {
+  const int64_t t = tt::backward::fused::T;
+  return (q_len + t - 1) / t * t;
+}
+
 TT_ATTN_API size_t tt_attn_backward_workspace_size(int64_t batch, int64_t heads, int64_t q_len) {
   if (batch <= 0 || heads <= 0 || q_len <= 0 || batch > INT32_MAX / heads || q_len > INT32_MAX)
     return 0;
-  return static_cast<size_t>(batch * heads) * static_cast<size_t>(q_len) * sizeof(float);
+  const int64_t bh = batch * heads;
+  return 2 * static_cast<size_t>(bh * backward_q_pad(q_len)) * sizeof(float) +
+         static_cast<size_t>(bh * q_len) * TT_ATTN_HEAD_DIM * sizeof(float);
 }
 
 TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
@@ -352,10 +392,12 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   if (batch > INT32_MAX / heads)
     return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
   const int64_t bh = batch * heads;
-  const int64_t q_tiles = (q_len + tt::backward::TILE - 1) / tt::backward::TILE;
-  const int64_t k_tiles = (kv_len + tt::backward::TILE - 1) / tt::backward::TILE;
-  const int64_t rows = bh * q_len;
-  if (q_tiles > INT32_MAX / bh || k_tiles > INT32_MAX / bh || (rows + 7) / 8 > INT32_MAX)
+  const int64_t k_tiles = (kv_len + tt::backward::fused::T - 1) / tt::backward::fused::T;
+  const int64_t q_pad = backward_q_pad(q_len);
+  const int64_t rows = bh * q_len, pad_rows = bh * q_pad;
+  if (k_tiles > INT32_MAX / bh ||
+      (pad_rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK >
+          INT32_MAX)
     return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
   const Shape4 qs = canonical(batch, heads, q_len, q_strides);
   const Shape4 ks = canonical(batch, heads, kv_len, k_strides);
@@ -372,59 +414,73 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   if (reinterpret_cast<uintptr_t>(lse) % 4 != 0)
     return fail(TT_ATTN_BAD_ARG, "LSE must be 4-byte aligned");
   const size_t ws_needed = tt_attn_backward_workspace_size(batch, heads, q_len);
-  if (workspace == nullptr || workspace_bytes < ws_needed ||
-      reinterpret_cast<uintptr_t>(workspace) % 4 != 0)
-    return fail(TT_ATTN_BAD_ARG, "workspace is smaller than tt_attn_backward_workspace_size()");
+  if (workspace == nullptr || workspace_bytes < ws_needed || !aligned16(workspace))
+    return fail(TT_ATTN_BAD_ARG, "workspace is smaller than tt_attn_backward_workspace_size() "
+                                 "or not 16-byte aligned");
 
   int dev = 0;
   tt_attn_status st = prepare_device(&dev);
   if (st != TT_ATTN_OK) return st;
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  float* D = static_cast<float*>(workspace);
-
-  tt::backward::PreParams pp{};
-  pp.rows = rows;
-  pp.dO = static_cast<const __nv_bfloat16*>(dout);
-  pp.O = static_cast<const __nv_bfloat16*>(out);
-  pp.D = D;
-  const int64_t pre_blocks =
-      (rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK;
-  tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>(pre_blocks), 256, 0, cs>>>(pp);
-  if ((st = check_launch("bwd_preprocess_kernel launch")) != TT_ATTN_OK) return st;
+  float* nlse2 = static_cast<float*>(workspace);
+  float* nd = nlse2 + pad_rows;
+  float* dq_acc = nd + pad_rows;
+  const size_t acc_bytes = static_cast<size_t>(rows) * TT_ATTN_HEAD_DIM * sizeof(float);
 
   const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
                            TT_ATTN_HEAD_DIM, 1};
   const Shape4 dos = canonical(batch, heads, q_len, cstr);
-  // The dQ kernel reads Q / dO in 128-row tiles and K / V in 64-row steps; the dK/dV kernel
-  // the other way round.
-  constexpr unsigned tile = tt::backward::TILE, step = tt::backward::STEP;
-  CUtensorMap tmq_t, tmdo_t, tmk_s, tmv_s, tmq_s, tmdo_s, tmk_t, tmv_t;
+  constexpr unsigned tile = tt::backward::fused::T;
+  CUtensorMap tmq, tmdo, tmk, tmv, tmacc;
   std::string err;
-  if (!encode_map(&tmq_t, q, qs, &err, tile) || !encode_map(&tmdo_t, dout, dos, &err, tile) ||
-      !encode_map(&tmk_s, k, ks, &err, step) || !encode_map(&tmv_s, v, vs, &err, step) ||
-      !encode_map(&tmq_s, q, qs, &err, step) || !encode_map(&tmdo_s, dout, dos, &err, step) ||
-      !encode_map(&tmk_t, k, ks, &err, tile) || !encode_map(&tmv_t, v, vs, &err, tile))
+  if (!encode_map(&tmq, q, qs, &err, tile) || !encode_map(&tmdo, dout, dos, &err, tile) ||
+      !encode_map(&tmk, k, ks, &err, tile) || !encode_map(&tmv, v, vs, &err, tile) ||
+      !encode_map_f32(&tmacc, dq_acc, dos, &err, tt::backward::fused::DQ_BOX_ROWS))
     return fail(TT_ATTN_UNSUPPORTED, err);
 
-  tt::backward::Params p{};
+  cudaError_t e = cudaMemsetAsync(dq_acc, 0, acc_bytes, cs);
+  if (e != cudaSuccess)
+    return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+
+  tt::backward::PreParams pp{};
+  pp.rows = pad_rows;
+  pp.Tq = static_cast<int>(q_len);
+  pp.Tq_pad = static_cast<int>(q_pad);
+  pp.dO = static_cast<const __nv_bfloat16*>(dout);
+  pp.O = static_cast<const __nv_bfloat16*>(out);
+  pp.lse = lse;
+  pp.nlse2 = nlse2;
+  pp.nd = nd;
+  const int64_t pre_blocks =
+      (pad_rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK;
+  tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>(pre_blocks), 256, 0, cs>>>(pp);
+  if ((st = check_launch("bwd_preprocess_kernel launch")) != TT_ATTN_OK) return st;
+
+  tt::backward::fused::Params p{};
   p.B = static_cast<int>(batch);
   p.H = static_cast<int>(heads);
   p.Tq = static_cast<int>(q_len);
   p.Tk = static_cast<int>(kv_len);
   p.past_len = static_cast<int>(past_len);
-  p.lse = lse;
-  p.D = D;
-  p.n_tiles = static_cast<int>(q_tiles);
-  p.out0 = static_cast<__nv_bfloat16*>(dq);
-  tt::backward::bwd_dq_kernel<<<static_cast<unsigned>(bh * q_tiles), tt::backward::THREADS,
-                                tt::backward::kSmemQ, cs>>>(tmq_t, tmk_s, tmv_s, tmdo_t, p);
-  if ((st = check_launch("bwd_dq_kernel launch")) != TT_ATTN_OK) return st;
-  p.n_tiles = static_cast<int>(k_tiles);
-  p.out0 = static_cast<__nv_bfloat16*>(dk);
-  p.out1 = static_cast<__nv_bfloat16*>(dv);
-  tt::backward::bwd_dkdv_kernel<<<static_cast<unsigned>(bh * k_tiles), tt::backward::THREADS,
-                                  tt::backward::kSmemKV, cs>>>(tmq_s, tmk_t, tmv_t, tmdo_s, p);
-  return check_launch("bwd_dkdv_kernel launch");
+  p.n_k_tiles = static_cast<int>(k_tiles);
+  p.Tq_pad = static_cast<int>(q_pad);
+  p.nlse2 = nlse2;
+  p.nd = nd;
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  tt::backward::fused::bwd_fused_kernel<<<static_cast<unsigned>(bh * k_tiles),
+                                          tt::backward::fused::THREADS,
+                                          tt::backward::fused::kSmemBytes, cs>>>(
+      tmq, tmk, tmv, tmdo, tmacc, p);
+  if ((st = check_launch("bwd_fused_kernel launch")) != TT_ATTN_OK) return st;
+
+  tt::backward::fused::ConvertParams cp{};
+  cp.rows = rows;
+  cp.acc = dq_acc;
+  cp.dq = static_cast<__nv_bfloat16*>(dq);
+  const int64_t conv_blocks = (rows * (TT_ATTN_HEAD_DIM / 8) + 255) / 256;
+  tt::backward::fused::bwd_dq_convert_kernel<<<static_cast<unsigned>(conv_blocks), 256, 0, cs>>>(cp);
+  return check_launch("bwd_dq_convert_kernel launch");
 }
 
 TT_ATTN_API tt_attn_status tt_attn_selftest_wait_timeout(int64_t budget_cycles, void* stream) {
