@@ -97,8 +97,7 @@ __device__ __forceinline__ int chunks_for(int L, int chunk) {
   return L <= 0 ? 1 : (L + chunk - 1) / chunk;
 }
 
-__device__ __forceinline__ void load_row8(const uint8_t* src, float (&f)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ void unpack_row8(const uint4 u, float (&f)[8]) {
   f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x);
   f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
   f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z);
@@ -256,7 +255,7 @@ decode_split_kernel(const Params p) {
         const uint8_t* qrow = reinterpret_cast<const uint8_t*>(p.q + b * p.q_sb + h * p.q_sh);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-          load_row8(qrow + ((cc + lane) & 7) * 16, qr[cc]);
+          unpack_row8(*reinterpret_cast<const uint4*>(qrow + ((cc + lane) & 7) * 16), qr[cc]);
 #pragma unroll
           for (int e = 0; e < 8; ++e) qr[cc][e] *= p.scale_log2;
         }
@@ -264,8 +263,10 @@ decode_split_kernel(const Params p) {
         l = 0.f;
         a0 = a1 = 0.f;
       }
-      const uint8_t* ks = s.ring[r.st] + row0 * ROW_BYTES;
-      const uint8_t* vs = s.ring[r.st] + (SUB + row0) * ROW_BYTES;
+      // Ring reads use explicit shared-memory loads (ld.shared): through the re-aligned Smem
+      // pointer the compiler would emit generic loads, measured 3.6 % slower on cfg4.
+      const uint32_t ks = smem_u32(s.ring[r.st]) + row0 * ROW_BYTES;
+      const uint32_t vs = smem_u32(s.ring[r.st]) + (SUB + row0) * ROW_BYTES;
       const int r_valid = max(0, min(SUB, hd.rows - hd.sub * SUB)) - row0;  // this warp's rows
 
       float x = -INFINITY;  // score of this lane's row
@@ -274,7 +275,7 @@ decode_split_kernel(const Params p) {
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           float kf[8];
-          load_row8(ks + lane * ROW_BYTES + ((cc + lane) & 7) * 16, kf);
+          unpack_row8(lds_u4(ks + lane * ROW_BYTES + ((cc + lane) & 7) * 16), kf);
 #pragma unroll
           for (int e = 0; e < 8; ++e) d[e & 3] = fmaf(qr[cc][e], kf[e], d[e & 3]);
         }
@@ -289,21 +290,26 @@ decode_split_kernel(const Params p) {
         const float pr = ex2_approx(x - m_new);  // invalid rows: exp2(-inf) = 0
         l = l * f + pr;
         float b0[4] = {a0 * f, 0.f, 0.f, 0.f}, b1[4] = {a1 * f, 0.f, 0.f, 0.f};
-        const uint8_t* vcol = vs + lane * 4;
+        const uint32_t vcol = vs + lane * 4;
         if (r_valid >= ROWS_PER_WARP) {
 #pragma unroll
           for (int rr = 0; rr < ROWS_PER_WARP; ++rr) {
             const float pb = __shfl_sync(0xffffffffu, pr, rr);
-            const uint32_t vv = *reinterpret_cast<const uint32_t*>(vcol + rr * ROW_BYTES);
+            const uint32_t vv = lds_u32(vcol + rr * ROW_BYTES);
             b0[rr & 3] = fmaf(pb, bf16_lo(vv), b0[rr & 3]);
             b1[rr & 3] = fmaf(pb, bf16_hi(vv), b1[rr & 3]);
           }
         } else {
-          for (int rr = 0; rr < r_valid; ++rr) {
-            const float pb = __shfl_sync(0xffffffffu, pr, rr);
-            const uint32_t vv = *reinterpret_cast<const uint32_t*>(vcol + rr * ROW_BYTES);
-            b0[rr & 3] = fmaf(pb, bf16_lo(vv), b0[rr & 3]);
-            b1[rr & 3] = fmaf(pb, bf16_hi(vv), b1[rr & 3]);
+          // Tail of a sequence: the same loop under a warp-uniform guard (unrolled, so the
+          // accumulator indices stay static and in registers).
+#pragma unroll
+          for (int rr = 0; rr < ROWS_PER_WARP; ++rr) {
+            if (rr < r_valid) {
+              const float pb = __shfl_sync(0xffffffffu, pr, rr);
+              const uint32_t vv = lds_u32(vcol + rr * ROW_BYTES);
+              b0[rr & 3] = fmaf(pb, bf16_lo(vv), b0[rr & 3]);
+              b1[rr & 3] = fmaf(pb, bf16_hi(vv), b1[rr & 3]);
+            }
           }
         }
         a0 = (b0[0] + b0[1]) + (b0[2] + b0[3]);
