@@ -115,6 +115,7 @@ def _bwd(lib, *, q=16, k=16, v=16, do=16, o=16, lse=16, dq=16, dk=16, dv=16, B=1
     (dict(tk=5), "Tk == past_len + Tq"),
     (dict(tq=2**31, tk=2**31), "int32"),
     (dict(B=2**20, H=2**12), "grid limits"),
+    (dict(tq=2**31 - 64, tk=2**31 - 64), "grid limits"),  # rows padded to 128 exceed int32
     (dict(dq=24), "16-byte"),
     (dict(lse=18), "4-byte"),
     (dict(ws_bytes=4), "workspace"),

@@ -395,9 +395,11 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   const int64_t k_tiles = (kv_len + tt::backward::fused::T - 1) / tt::backward::fused::T;
   const int64_t q_pad = backward_q_pad(q_len);
   const int64_t rows = bh * q_len, pad_rows = bh * q_pad;
-  if (k_tiles > INT32_MAX / bh ||
+  // Query rows padded to whole tiles are int32 in the kernels; every grid must fit int32.
+  if (q_pad > INT32_MAX || k_tiles > INT32_MAX / bh ||
       (pad_rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK >
-          INT32_MAX)
+          INT32_MAX ||
+      (rows * (TT_ATTN_HEAD_DIM / 8) + 255) / 256 > INT32_MAX)
     return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
   const Shape4 qs = canonical(batch, heads, q_len, q_strides);
   const Shape4 ks = canonical(batch, heads, kv_len, k_strides);
