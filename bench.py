@@ -286,6 +286,14 @@ def run_ours(args):
         barrier(world)
         torch.cuda.synchronize()
         bwd_ms = reduce_max(sum(times) / len(times), world)
+        # The fixed-order path taken under torch.use_deterministic_algorithms(True) (this rank).
+        det_mode = (torch.are_deterministic_algorithms_enabled(),
+                    torch.is_deterministic_algorithms_warn_only_enabled())
+        torch.use_deterministic_algorithms(True)
+        try:
+            det_ms = sum(time_device(torch, fn, bsteps, args.warmup, flush)) / bsteps
+        finally:
+            torch.use_deterministic_algorithms(det_mode[0], warn_only=det_mode[1])
         with torch.enable_grad():
             qq, kk, vv = [x.detach().requires_grad_() for x in (q, k, v)]
             o2 = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True)
@@ -305,6 +313,8 @@ def run_ours(args):
             "gpu_launches": 3 * bsteps,
             "sdpa": {"value": round(bwd_flops / (sdpa_bwd_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                      "ms_per_step": round(sdpa_bwd_ms, 4)},
+            "deterministic": {"value": round(bwd_flops / (det_ms * 1e-3) / 1e12, 2),
+                              "unit": "TFLOP/s", "ms_per_step": round(det_ms, 4)},
         }
         del q, k, v, out, lse, dout
 

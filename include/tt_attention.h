@@ -127,6 +127,21 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
     int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
     void* stream);
 
+/*
+ * Same contract as tt_attn_backward_bf16, with bit-identical results on every call: each output
+ * element is accumulated by one CTA in a fixed order (three kernels: row sums D, a dQ kernel
+ * over 128-row query tiles, a dK/dV kernel over 128-key tiles), where tt_attn_backward_bf16
+ * adds the dQ contributions of different key tiles with reduce-adds in timing-dependent order.
+ * The torch binding takes this path under torch.use_deterministic_algorithms(True); the
+ * reference's own backward kernels use no atomics. Same workspace size.
+ */
+TT_ATTN_API tt_attn_status tt_attn_backward_bf16_deterministic(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, const void* dout, const void* out, const float* lse,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
+    int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+    void* stream);
+
 /* Bytes of workspace tt_attn_backward_bf16 needs (batch * heads * q_len FP32 row sums, padded
  * to 256 bytes, plus batch * heads * q_len * 64 FP32 for dQ), 0 for invalid sizes. */
 TT_ATTN_API size_t tt_attn_backward_workspace_size(int64_t batch, int64_t heads, int64_t q_len);

@@ -100,11 +100,11 @@ def test_workspace_and_layout_queries(lib):
 
 
 def _bwd(lib, *, q=16, k=16, v=16, do=16, o=16, lse=16, dq=16, dk=16, dv=16, B=1, H=1, tq=4,
-         tk=4, d=64, past=0, ws=256, ws_bytes=1 << 20):
+         tk=4, d=64, past=0, ws=256, ws_bytes=1 << 20, entry="tt_attn_backward_bf16"):
     qs = _strides(tq * 64 * H, tq * 64, 64, 1)
     ks = _strides(tk * 64 * H, tk * 64, 64, 1)
-    return lib.tt_attn_backward_bf16(q, qs, k, ks, v, ks, do, o, lse, B, H, tq, tk, d, past,
-                                     dq, dk, dv, ws, ws_bytes, None)
+    return getattr(lib, entry)(q, qs, k, ks, v, ks, do, o, lse, B, H, tq, tk, d, past,
+                               dq, dk, dv, ws, ws_bytes, None)
 
 
 @pytest.mark.parametrize("kwargs,fragment", [
@@ -120,8 +120,9 @@ def _bwd(lib, *, q=16, k=16, v=16, do=16, o=16, lse=16, dq=16, dk=16, dv=16, B=1
     (dict(lse=18), "4-byte"),
     (dict(ws_bytes=4), "workspace"),
 ])
-def test_backward_rejects_bad_arguments_before_cuda(lib, kwargs, fragment):
-    assert _bwd(lib, **kwargs) == 1  # TT_ATTN_BAD_ARG
+@pytest.mark.parametrize("entry", ["tt_attn_backward_bf16", "tt_attn_backward_bf16_deterministic"])
+def test_backward_rejects_bad_arguments_before_cuda(lib, kwargs, fragment, entry):
+    assert _bwd(lib, entry=entry, **kwargs) == 1  # TT_ATTN_BAD_ARG
     assert fragment in _err(lib)
 
 

@@ -203,7 +203,12 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> attention_backward(
   const int64_t qs[4] = {q.stride(0), q.stride(1), q.stride(2), q.stride(3)};
   const int64_t ks[4] = {k.stride(0), k.stride(1), k.stride(2), k.stride(3)};
   const int64_t vs[4] = {v.stride(0), v.stride(1), v.stride(2), v.stride(3)};
-  const tt_attn_status st = tt_attn_backward_bf16(
+  // Under torch.use_deterministic_algorithms(True) take the fixed-order path (the fused kernel
+  // adds dQ contributions with reduce-adds in timing-dependent order).
+  const auto backward_fn = at::globalContext().deterministicAlgorithms()
+                               ? tt_attn_backward_bf16_deterministic
+                               : tt_attn_backward_bf16;
+  const tt_attn_status st = backward_fn(
       q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, dO.data_ptr(), O.data_ptr(),
       lse.data_ptr<float>(), B, H, Tq, Tk, TT_ATTN_HEAD_DIM, past_len, dq.data_ptr(),
       dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes, static_cast<void*>(stream.stream()));

@@ -21,6 +21,7 @@
 #include "selftest_sm100.cuh"
 #include "rope_append_sm100.cuh"
 #include "backward_sm100.cuh"
+#include "backward_det_sm100.cuh"
 
 namespace {
 
@@ -225,6 +226,14 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
       e = cudaFuncSetAttribute(tt::backward::fused::bwd_fused_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tt::backward::fused::kSmemBytes));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tt::backward_det::bwd_dq_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tt::backward_det::kSmemQ));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tt::backward_det::bwd_dkdv_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tt::backward_det::kSmemKV));
     if (e != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     ds.attrs_set = true;
@@ -369,12 +378,75 @@ TT_ATTN_API size_t tt_attn_backward_workspace_size(int64_t batch, int64_t heads,
          static_cast<size_t>(bh * q_len) * TT_ATTN_HEAD_DIM * sizeof(float);
 }
 
-TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
-    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
-    const void* v, const int64_t* v_strides, const void* dout, const void* out, const float* lse,
-    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
-    int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
-    void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The deterministic backward: row sums D (first bh * Tq floats of the workspace), then the dQ
+// kernel (128-row query tiles over 64-key steps) and the dK/dV kernel (128-key tiles over
+// 64-row query steps); each output element is accumulated by one CTA in a fixed order.
+tt_attn_status backward_deterministic(const void* q, const void* k, const void* v,
+                                      const void* dout, const void* out, const float* lse,
+                                      const Shape4& qs, const Shape4& ks, const Shape4& vs,
+                                      const Shape4& dos, int64_t batch, int64_t heads,
+                                      int64_t q_len, int64_t kv_len, int64_t past_len, void* dq,
+                                      void* dk, void* dv, float* D, cudaStream_t cs) {
+  namespace det = tt::backward_det;
+  const int64_t bh = batch * heads;
+  const int64_t rows = bh * q_len;
+  const int64_t q_tiles = (q_len + det::TILE - 1) / det::TILE;
+  const int64_t k_tiles = (kv_len + det::TILE - 1) / det::TILE;
+  if (q_tiles > INT32_MAX / bh)
+    return fail(TT_ATTN_BAD_ARG, "attention backward shape exceeds the supported CUDA grid limits");
+  det::PreParams pp{};
+  pp.rows = rows;
+  pp.dO = static_cast<const __nv_bfloat16*>(dout);
+  pp.O = static_cast<const __nv_bfloat16*>(out);
+  pp.D = D;
+  const int64_t pre_blocks = (rows + det::PRE_ROWS_PER_BLOCK - 1) / det::PRE_ROWS_PER_BLOCK;
+  det::bwd_preprocess_kernel<<<static_cast<unsigned>(pre_blocks), 256, 0, cs>>>(pp);
+  tt_attn_status st = check_launch("bwd_preprocess_kernel (deterministic) launch");
+  if (st != TT_ATTN_OK) return st;
+  // The dQ kernel reads Q / dO in 128-row tiles and K / V in 64-row steps; the dK/dV kernel
+  // the other way round.
+  constexpr unsigned tile = det::TILE, step = det::STEP;
+  CUtensorMap tmq_t, tmdo_t, tmk_s, tmv_s, tmq_s, tmdo_s, tmk_t, tmv_t;
+  std::string err;
+  if (!encode_map(&tmq_t, q, qs, &err, tile) || !encode_map(&tmdo_t, dout, dos, &err, tile) ||
+      !encode_map(&tmk_s, k, ks, &err, step) || !encode_map(&tmv_s, v, vs, &err, step) ||
+      !encode_map(&tmq_s, q, qs, &err, step) || !encode_map(&tmdo_s, dout, dos, &err, step) ||
+      !encode_map(&tmk_t, k, ks, &err, tile) || !encode_map(&tmv_t, v, vs, &err, tile))
+    return fail(TT_ATTN_UNSUPPORTED, err);
+  det::Params p{};
+  p.B = static_cast<int>(batch);
+  p.H = static_cast<int>(heads);
+  p.Tq = static_cast<int>(q_len);
+  p.Tk = static_cast<int>(kv_len);
+  p.past_len = static_cast<int>(past_len);
+  p.lse = lse;
+  p.D = D;
+  p.n_tiles = static_cast<int>(q_tiles);
+  p.out0 = static_cast<__nv_bfloat16*>(dq);
+  det::bwd_dq_kernel<<<static_cast<unsigned>(bh * q_tiles), det::THREADS, det::kSmemQ, cs>>>(
+      tmq_t, tmk_s, tmv_s, tmdo_t, p);
+  if ((st = check_launch("bwd_dq_kernel launch")) != TT_ATTN_OK) return st;
+  p.n_tiles = static_cast<int>(k_tiles);
+  p.out0 = static_cast<__nv_bfloat16*>(dk);
+  p.out1 = static_cast<__nv_bfloat16*>(dv);
+  det::bwd_dkdv_kernel<<<static_cast<unsigned>(bh * k_tiles), det::THREADS, det::kSmemKV, cs>>>(
+      tmq_s, tmk_t, tmv_t, tmdo_s, p);
+  return check_launch("bwd_dkdv_kernel launch");
+}
+
+// Both backward entry points: shared validation, then the fused path (dQ contributions of
+// different key tiles added with reduce-adds in timing-dependent order) or the deterministic
+// two-kernel path.
+tt_attn_status backward_impl(
+    bool deterministic, const void* q, const int64_t* q_strides, const void* k,
+    const int64_t* k_strides, const void* v, const int64_t* v_strides, const void* dout,
+    const void* out, const float* lse, int64_t batch, int64_t heads, int64_t q_len,
+    int64_t kv_len, int64_t head_dim, int64_t past_len, void* dq, void* dk, void* dv,
+    void* workspace, size_t workspace_bytes, void* stream) {
   // ---- validation: everything is checked before any CUDA call
   if (!q || !k || !v || !dout || !out || !lse || !dq || !dk || !dv || !q_strides || !k_strides ||
       !v_strides)
@@ -424,14 +496,17 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   tt_attn_status st = prepare_device(&dev);
   if (st != TT_ATTN_OK) return st;
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
+                           TT_ATTN_HEAD_DIM, 1};
+  const Shape4 dos = canonical(batch, heads, q_len, cstr);
+  if (deterministic)
+    return backward_deterministic(q, k, v, dout, out, lse, qs, ks, vs, dos, batch, heads, q_len,
+                                  kv_len, past_len, dq, dk, dv, static_cast<float*>(workspace), cs);
   float* nlse2 = static_cast<float*>(workspace);
   float* nd = nlse2 + pad_rows;
   float* dq_acc = nd + pad_rows;
   const size_t acc_bytes = static_cast<size_t>(rows) * TT_ATTN_HEAD_DIM * sizeof(float);
 
-  const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
-                           TT_ATTN_HEAD_DIM, 1};
-  const Shape4 dos = canonical(batch, heads, q_len, cstr);
   constexpr unsigned tile = tt::backward::fused::T;
   CUtensorMap tmq, tmdo, tmk, tmv, tmacc;
   std::string err;
@@ -483,6 +558,32 @@ TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
   const int64_t conv_blocks = (rows * (TT_ATTN_HEAD_DIM / 8) + 255) / 256;
   tt::backward::fused::bwd_dq_convert_kernel<<<static_cast<unsigned>(conv_blocks), 256, 0, cs>>>(cp);
   return check_launch("bwd_dq_convert_kernel launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, const void* dout, const void* out, const float* lse,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
+    int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  return backward_impl(false, q, q_strides, k, k_strides, v, v_strides, dout, out, lse, batch,
+                       heads, q_len, kv_len, head_dim, past_len, dq, dk, dv, workspace,
+                       workspace_bytes, stream);
+}
+
+TT_ATTN_API tt_attn_status tt_attn_backward_bf16_deterministic(
+    const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+    const void* v, const int64_t* v_strides, const void* dout, const void* out, const float* lse,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, int64_t head_dim,
+    int64_t past_len, void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  return backward_impl(true, q, q_strides, k, k_strides, v, v_strides, dout, out, lse, batch,
+                       heads, q_len, kv_len, head_dim, past_len, dq, dk, dv, workspace,
+                       workspace_bytes, stream);
 }
 
 TT_ATTN_API tt_attn_status tt_attn_selftest_wait_timeout(int64_t budget_cycles, void* stream) {

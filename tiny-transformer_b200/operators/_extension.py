@@ -59,6 +59,8 @@ def load_c_abi() -> ctypes.CDLL:
         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_size_t, ctypes.c_void_p]
+    lib.tt_attn_backward_bf16_deterministic.restype = ctypes.c_int
+    lib.tt_attn_backward_bf16_deterministic.argtypes = lib.tt_attn_backward_bf16.argtypes
     lib.tt_attn_backward_workspace_size.restype = ctypes.c_size_t
     lib.tt_attn_backward_workspace_size.argtypes = [ctypes.c_int64] * 3
     lib.tt_rope_append_bf16.restype = ctypes.c_int
