@@ -213,6 +213,11 @@ def run_ours(args):
     def flush():
         flush_buf.fill_(1)
 
+    def busy():
+        # A ~50 us spin kernel with no memory traffic: the GPU is still busy while the host
+        # enqueues the timed step, so host launch latency stays outside the events.
+        torch.cuda._sleep(100_000)
+
     results = {}
     with torch.no_grad():
         # ------------------------------------------------------------------ prefill (cfg 3)
@@ -326,12 +331,17 @@ def run_ours(args):
         fn = lambda: ext.attention_forward(q, k, v, c["Tk"] - 1, None, lens)  # noqa: E731
         barrier(world)
         torch.cuda.synchronize()
+        # The K/V read (~0.9 GB) is 7x L2, so the headline uses no flush: a 256 MiB flush write
+        # leaves up to L2's worth of dirty lines whose write-back would land inside the timed
+        # step. The flushed timing is reported beside it.
         with ClockSampler(local) as clk:
-            times = time_device(torch, fn, args.steps, args.warmup, flush)
+            times = time_device(torch, fn, args.steps, args.warmup, busy)
+            flushed = time_device(torch, fn, args.steps, args.warmup, flush)
             barrier(world)
             torch.cuda.synchronize()
         kernel_ms = sum(times) / len(times)
         step_ms = reduce_max(kernel_ms, world)
+        flushed_ms = reduce_max(sum(flushed) / len(flushed), world)
         # e2e: the cache lives on the device (it is the model's KV cache); per step the host
         # sends q and the lengths and reads back O and LSE.
         hq = q.cpu().pin_memory()
@@ -359,7 +369,8 @@ def run_ours(args):
                        "global_batch": c["B"] * world, "heads": c["H"], "kv_capacity": c["Tk"],
                        "sum_kv_lens_rank0": int(lens_np.sum()), "algorithmic_bytes": nbytes,
                        "parallelism": f"batch shards, {world} rank(s)",
-                       "l2": "flushed between timed steps; K/V read (~0.9 GB) exceeds L2"},
+                       "l2": "inputs larger than L2 (K/V read ~0.9 GB, 7x L2), no flush; a "
+                             "spin kernel ahead of each step keeps host latency out"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_kind": f"{peaks['source']} copy bandwidth", "traffic": tr,
@@ -368,7 +379,10 @@ def run_ours(args):
                     "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": hq.numel() * 2 + hlens.numel() * 4,
                     "d2h_bytes_per_step": ho.numel() * 2 + hl.numel() * 4},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,
+            "flushed": {"value": round(world * nbytes / (flushed_ms * 1e-3) / 1e9, 1),
+                        "ms_per_step": round(flushed_ms, 4),
+                        "l2": "256 MiB write between timed steps"},
             "clocks": clk.summary(),
         }
 

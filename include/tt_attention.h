@@ -58,8 +58,9 @@ typedef enum tt_attn_status {
  *   lse      contiguous [batch, heads, q_len] fp32, natural log
  *   workspace / workspace_bytes: device scratch of at least
  *            tt_attn_forward_workspace_size(...) bytes (may be NULL when that is 0). Decode
- *            (q_len == 1) keeps a work counter there, which the call zeroes on `stream`
- *            before its kernels run, and its split-KV partials.
+ *            (q_len == 1) keeps a work counter and per-sequence arrival counters there,
+ *            which the call zeroes on `stream` before its kernel runs, and its split-KV
+ *            partials.
  *   stream   cudaStream_t the kernels are launched on; no host synchronisation.
  *
  * Layout requirements (else TT_ATTN_UNSUPPORTED): last stride 1, other strides positive
@@ -76,8 +77,10 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     void* stream);
 
 /* Scratch bytes tt_attn_forward_bf16 needs for this shape: for decode, a 256-byte work
- * counter plus the split-KV partials. Replaces the partials tensor the reference allocates
- * (attention.cu:128-129). Returns 0 for prefill shapes and for invalid shapes. */
+ * counter, plus (when sequences are split into more than one chunk) one 4-byte arrival counter
+ * per (batch, head) rounded up to 256 bytes and 272 bytes of FP32 partial per (batch, head,
+ * chunk). Replaces the partials tensor the reference allocates (attention.cu:128-129).
+ * Returns 0 for prefill shapes and for invalid shapes. */
 TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, int64_t q_len,
                                                   int64_t kv_len);
 

@@ -439,11 +439,14 @@ def test_rejects_sequence_index_overflow_before_copy(ext):
 def test_decode_work_item_sizes(ext, tk, chunk):
     """Enough heads (50 x 12) that the host picks 768- and 1536-key work items: sequence ends on
     and beside item boundaries, with and without kv_lens. The chosen item size is read back
-    from the workspace the C ABI asks for (a counter plus one 272-byte partial per item)."""
+    from the workspace the C ABI asks for (a work counter, one arrival counter per (batch, head)
+    rounded up to 256 bytes, and one 272-byte partial per item)."""
     from tiny_transformer_b200.operators._extension import load_c_abi
     B, H = 50, 12
     n_items = -(-tk // chunk)
-    assert load_c_abi().tt_attn_forward_workspace_size(B, H, 1, tk) == 256 + B * H * n_items * 272
+    arrivals = -(-B * H * 4 // 256) * 256
+    assert (load_c_abi().tt_attn_forward_workspace_size(B, H, 1, tk)
+            == 256 + arrivals + B * H * n_items * 272)
     torch.manual_seed(tk)
     q = torch.randn(B, H, 1, 64, device="cuda", dtype=torch.bfloat16)
     k, v = [torch.randn(B, H, tk, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]

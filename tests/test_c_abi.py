@@ -85,7 +85,8 @@ def test_unsupported_layouts(lib):
 def test_workspace_and_layout_queries(lib):
     # Decode with enough keys splits into several chunks and needs partials.
     n = lib.tt_attn_forward_workspace_size(8, 12, 1, 4096)
-    assert n > 256 and (n - 256) % (68 * 4) == 0   # work counter + partials
+    arrivals = -(-8 * 12 * 4 // 256) * 256        # one counter per (batch, head), 256-B rounded
+    assert n > 256 + arrivals and (n - 256 - arrivals) % (68 * 4) == 0  # counters + partials
     assert lib.tt_attn_forward_workspace_size(8, 12, 1, 16) == 256  # one chunk: counter only
     assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # prefill needs none
     assert lib.tt_attn_forward_workspace_size(0, 12, 1, 512) == 0

@@ -19,10 +19,15 @@
 //   product of its row (16-byte shared reads rotated by lane so 32 rows hit distinct banks; q
 //   is held pre-rotated in registers), the warp takes one max per 32 rows, and for P.V each
 //   lane owns two output features and receives every p by shuffle. Each warp keeps an online
-//   softmax (m, l, acc); at the end of an item the warps merge through a double-buffered
-//   shared record merged by warp 0.
-// An item that covers a whole sequence writes O and LSE; otherwise it writes an FP32 partial
-// (acc[64], m, l) that decode_combine_kernel merges. Every wait is a bounded mbarrier wait.
+//   softmax (m, l, acc); at the end of an item each warp leaves its (m, l, acc) in a
+//   double-buffered shared record and moves on to the next stage;
+// * a combine warp merges the 12 records of each item. An item that covers a whole sequence
+//   writes O and LSE; otherwise the combine warp writes an FP32 partial (acc[64], m, l),
+//   publishes it (release fence, then an arrival on the sequence's counter in the workspace)
+//   and, when its arrival is the sequence's last, merges all of the sequence's partials
+//   (acquire fence, L2 reads) into O and LSE. The split and the merge are one launch, and the
+//   streaming warps never wait for a global-memory round trip.
+// Every wait is a bounded mbarrier wait; no CTA waits for another CTA.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -41,12 +46,15 @@ constexpr int SUB = CONSUMER_WARPS * ROWS_PER_WARP;  // 384 key rows per ring st
 constexpr int STAGES = 2;
 constexpr int STAGE_BYTES = 2 * SUB * ROW_BYTES;     // K then V rows: 96 KiB
 constexpr int PRODUCER_WARP = CONSUMER_WARPS;
-constexpr int THREADS = (CONSUMER_WARPS + 1) * 32;
+constexpr int COMBINE_WARP = CONSUMER_WARPS + 1;
+constexpr int THREADS = (CONSUMER_WARPS + 2) * 32;
 constexpr int MIN_CHUNK = SUB;
 constexpr int MAX_CHUNK = 4 * SUB;                   // 1536 keys per work item
 constexpr int PARTIAL = HD + 4;                      // acc[64], m (log2 units), l, 2 pad:
                                                      // 272 B records keep float4 stores aligned
-constexpr size_t kCounterBytes = 256;                // work counter at the start of the workspace
+constexpr size_t kCounterBytes = 256;                // work counter at the start of the workspace,
+                                                     // then (split sequences only) one arrival
+                                                     // counter per (batch, head), 256-B rounded
 constexpr float LN2 = 0.69314718055994530942f;
 
 struct StageHeader {
@@ -58,9 +66,17 @@ struct StageHeader {
   int nc;    // chunks of this sequence
 };
 
+struct ItemHeader {
+  int bh;  // batch * heads + head; -1 ends the combine warp's loop
+  int ch;  // chunk of the item
+  int nc;  // chunks of this sequence
+  int pad;
+};
+
 struct alignas(128) Smem {
   uint8_t ring[STAGES][STAGE_BYTES];
   float red[2][CONSUMER_WARPS][PARTIAL];  // per-warp item records, double-buffered
+  ItemHeader item[2];                     // the item each record buffer holds
   StageHeader hdr[STAGES];
   uint64_t full[STAGES], empty[STAGES];
   uint64_t red_full[2], red_free[2];
@@ -83,6 +99,8 @@ struct Params {
   __nv_bfloat16* o;            // contiguous [B,H,1,64]
   float* lse;                  // [B,H,1]
   unsigned* counter;           // next work item (zero at launch)
+  unsigned* arrivals;          // [B*H] partials written per sequence (zero at launch; used
+                               // when n_chunks > 1)
   float* partials;             // [B*H, n_chunks, PARTIAL] (used when n_chunks > 1)
   float scale_log2;
 };
@@ -213,6 +231,102 @@ __device__ __forceinline__ void produce(Smem& s, const Params& p, int lane) {
   }
 }
 
+// Merge all partials of sequence bh (called by one warp once every chunk's partial is
+// published): lane c reads chunk c's (m, l), the warp reduces the max, and each lane accumulates
+// two features over all chunks with the weights exp2(m_c - M) broadcast by shuffle (never
+// averages normalised outputs). The partials were written by other SMs, so they are read from
+// L2 (ld.global.cg), not through this SM's L1.
+__device__ __forceinline__ void merge_sequence(const Params& p, int bh, int nc, int lane) {
+  const float* src = p.partials + static_cast<size_t>(bh) * p.n_chunks * PARTIAL;
+  float M = -INFINITY;
+  for (int c = lane; c < nc; c += 32) M = fmaxf(M, __ldcg(src + c * PARTIAL + HD));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float n0 = 0.f, n1 = 0.f, den = 0.f;
+  for (int base = 0; base < nc; base += 32) {
+    const int c = base + lane;
+    float w = 0.f;
+    if (c < nc) {
+      const float mc = __ldcg(src + c * PARTIAL + HD);
+      w = (mc == -INFINITY) ? 0.f : ex2_approx(mc - M);
+      den = fmaf(w, __ldcg(src + c * PARTIAL + HD + 1), den);
+    }
+    const int cnt = min(32, nc - base);
+#pragma unroll 4
+    for (int i = 0; i < cnt; ++i) {
+      const float wi = __shfl_sync(0xffffffffu, w, i);
+      const float2 a = __ldcg(reinterpret_cast<const float2*>(src + (base + i) * PARTIAL) + lane);
+      n0 = fmaf(wi, a.x, n0);
+      n1 = fmaf(wi, a.y, n1);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  reinterpret_cast<uint32_t*>(p.o + static_cast<size_t>(bh) * HD)[lane] =
+      pack_bf16x2(n0 * inv, n1 * inv);
+  if (lane == 0) p.lse[bh] = den > 0.f ? (M + log2f(den)) * LN2 : -INFINITY;
+}
+
+// Combine warp: for each item, merge the CONSUMER_WARPS warp records (lane t owns features
+// 2t, 2t + 1), free the record buffer, then write O and LSE (whole sequence) or the item's
+// partial. A partial is published with a release fence before the arrival on the sequence's
+// counter; the warp whose arrival completes the count takes an acquire fence and merges the
+// sequence. Nothing here waits on another CTA.
+__device__ __forceinline__ void combine_items(Smem& s, const Params& p, int lane) {
+  unsigned items = 0;
+  while (true) {
+    const int buf = static_cast<int>(items & 1u);
+    const uint32_t use = items >> 1;
+    if (!warp_wait(s, &s.red_full[buf], use & 1)) break;
+    const ItemHeader it = s.item[buf];
+    if (it.bh < 0) break;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < CONSUMER_WARPS; ++w) M = fmaxf(M, s.red[buf][w][HD]);
+    float n0 = 0.f, n1 = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < CONSUMER_WARPS; ++w) {
+        const float mw = s.red[buf][w][HD];
+        if (mw == -INFINITY) continue;
+        const float wt = ex2_approx(mw - M);
+        const float2 a = reinterpret_cast<const float2*>(s.red[buf][w])[lane];
+        n0 = fmaf(wt, a.x, n0);
+        n1 = fmaf(wt, a.y, n1);
+        den = fmaf(wt, s.red[buf][w][HD + 1], den);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.red_free[buf]);
+    ++items;
+    if (it.nc == 1) {
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      reinterpret_cast<uint32_t*>(p.o + static_cast<size_t>(it.bh) * HD)[lane] =
+          pack_bf16x2(n0 * inv, n1 * inv);
+      if (lane == 0) p.lse[it.bh] = den > 0.f ? (M + log2f(den)) * LN2 : -INFINITY;
+      continue;
+    }
+    float* dst = p.partials + (static_cast<size_t>(it.bh) * p.n_chunks + it.ch) * PARTIAL;
+    reinterpret_cast<float2*>(dst)[lane] = make_float2(n0, n1);
+    if (lane == 0) {
+      dst[HD] = M;
+      dst[HD + 1] = den;
+    }
+    // Release: every lane's partial stores are ordered before the arrival.
+    __threadfence();
+    __syncwarp();
+    unsigned arrived = 0;
+    if (lane == 0) arrived = atomicAdd(p.arrivals + it.bh, 1u);
+    arrived = __shfl_sync(0xffffffffu, arrived, 0);
+    if (arrived + 1 == static_cast<unsigned>(it.nc)) {
+      // Acquire: the other chunks' partials, published before their arrivals, are visible.
+      __threadfence();
+      merge_sequence(p, it.bh, it.nc, lane);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
 decode_split_kernel(const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -237,7 +351,7 @@ decode_split_kernel(const Params p) {
 
   if (warp == PRODUCER_WARP) {
     produce(s, p, lane);
-  } else {
+  } else if (warp < CONSUMER_WARPS) {
     const int row0 = warp * ROWS_PER_WARP;
     Ring r;
     unsigned items = 0;    // items finished by this CTA
@@ -245,10 +359,14 @@ decode_split_kernel(const Params p) {
     float m = -INFINITY;   // warp-uniform running max (log2 units)
     float l = 0.f;         // this lane's share of the running sum
     float a0 = 0.f, a1 = 0.f;  // output features 2*lane, 2*lane + 1
+    bool ended = false;    // saw the producer's end-of-stream header
     while (true) {
       if (!warp_wait(s, &s.full[r.st], r.ph)) break;
       const StageHeader hd = s.hdr[r.st];
-      if (hd.bh < 0) break;
+      if (hd.bh < 0) {
+        ended = true;
+        break;
+      }
       if (hd.sub == 0) {
         // New item: rotated q and a fresh online softmax.
         const int b = hd.bh / p.H, h = hd.bh - b * p.H;
@@ -321,7 +439,8 @@ decode_split_kernel(const Params p) {
       r.next();
 
       if (hd.sub + 1 == hd.subs) {
-        // End of item: this warp's record (m, l, acc[64]) into a double-buffered shared slot.
+        // End of item: this warp's record (m, l, acc[64]) into a double-buffered shared slot
+        // for the combine warp.
         float lsum = l;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
@@ -333,98 +452,28 @@ decode_split_kernel(const Params p) {
         if (lane == 0) {
           rec[HD] = m;
           rec[HD + 1] = lsum;
+          if (warp == 0) s.item[buf] = ItemHeader{hd.bh, hd.ch, hd.nc, 0};
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.red_full[buf]);
-        if (warp == 0) {
-          if (!warp_wait(s, &s.red_full[buf], use & 1)) break;
-          // Lane t merges features 2t, 2t + 1 over the CONSUMER_WARPS warp records.
-          float M = -INFINITY;
-#pragma unroll
-          for (int w = 0; w < CONSUMER_WARPS; ++w) M = fmaxf(M, s.red[buf][w][HD]);
-          float n0 = 0.f, n1 = 0.f, den = 0.f;
-          if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < CONSUMER_WARPS; ++w) {
-              const float mw = s.red[buf][w][HD];
-              if (mw == -INFINITY) continue;
-              const float wt = ex2_approx(mw - M);
-              const float2 a = reinterpret_cast<const float2*>(s.red[buf][w])[lane];
-              n0 = fmaf(wt, a.x, n0);
-              n1 = fmaf(wt, a.y, n1);
-              den = fmaf(wt, s.red[buf][w][HD + 1], den);
-            }
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.red_free[buf]);
-          if (hd.nc == 1) {
-            const float inv = den > 0.f ? 1.f / den : 0.f;
-            reinterpret_cast<uint32_t*>(p.o + static_cast<size_t>(hd.bh) * HD)[lane] =
-                pack_bf16x2(n0 * inv, n1 * inv);
-            if (lane == 0) p.lse[hd.bh] = den > 0.f ? (M + log2f(den)) * LN2 : -INFINITY;
-          } else {
-            float* dst =
-                p.partials + (static_cast<size_t>(hd.bh) * p.n_chunks + hd.ch) * PARTIAL;
-            reinterpret_cast<float2*>(dst)[lane] = make_float2(n0, n1);
-            if (lane == 0) {
-              dst[HD] = M;
-              dst[HD + 1] = den;
-            }
-          }
-        }
         ++items;
       }
     }
+    if (ended) {
+      // End of stream for the combine warp: an item header with bh = -1.
+      const int buf = static_cast<int>(items & 1u);
+      const uint32_t use = items >> 1;
+      if (use == 0 || warp_wait(s, &s.red_free[buf], (use - 1) & 1)) {
+        if (lane == 0) {
+          if (warp == 0) s.item[buf].bh = -1;
+          mbar_arrive(&s.red_full[buf]);
+        }
+      }
+    }
+  } else {
+    combine_items(s, p, lane);
   }
   __syncthreads();
-  // Let the combine kernel (programmatic dependent launch) start its prologue.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// Merge the per-chunk partials of one (batch, head) per warp: lane c reads chunk c's (m, l),
-// the warp reduces the max, and each lane accumulates two features over all chunks with the
-// weights exp2(m_c - M) broadcast by shuffle (never averages normalised outputs).
-constexpr int COMBINE_WARPS = 4;
-
-__global__ void __launch_bounds__(COMBINE_WARPS * 32)
-decode_combine_kernel(const Params p) {
-  // Wait for the split kernel's partials (programmatic dependent launch).
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5);
-  if (bh >= p.B * p.H) return;
-  const int L = valid_len(p, bh / p.H);
-  const int nc = chunks_for(L, p.chunk);
-  if (nc <= 1) return;  // written directly by the split kernel
-  const float* src = p.partials + static_cast<size_t>(bh) * p.n_chunks * PARTIAL;
-  float M = -INFINITY;
-  for (int c = lane; c < nc; c += 32) M = fmaxf(M, src[c * PARTIAL + HD]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float n0 = 0.f, n1 = 0.f, den = 0.f;
-  for (int base = 0; base < nc; base += 32) {
-    const int c = base + lane;
-    float w = 0.f;
-    if (c < nc) {
-      const float mc = src[c * PARTIAL + HD];
-      w = (mc == -INFINITY) ? 0.f : ex2_approx(mc - M);
-      den = fmaf(w, src[c * PARTIAL + HD + 1], den);
-    }
-    const int cnt = min(32, nc - base);
-#pragma unroll 4
-    for (int i = 0; i < cnt; ++i) {
-      const float wi = __shfl_sync(0xffffffffu, w, i);
-      const float2 a = reinterpret_cast<const float2*>(src + (base + i) * PARTIAL)[lane];
-      n0 = fmaf(wi, a.x, n0);
-      n1 = fmaf(wi, a.y, n1);
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-  const float inv = den > 0.f ? 1.f / den : 0.f;
-  reinterpret_cast<uint32_t*>(p.o + static_cast<size_t>(bh) * HD)[lane] =
-      pack_bf16x2(n0 * inv, n1 * inv);
-  if (lane == 0) p.lse[bh] = den > 0.f ? (M + log2f(den)) * LN2 : -INFINITY;
 }
 
 }  // namespace decode

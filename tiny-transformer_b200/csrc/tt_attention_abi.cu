@@ -72,6 +72,12 @@ int decode_chunk(int64_t bh, int64_t tk) {
   return chunk;
 }
 
+// Bytes of the per-sequence arrival counters of a split decode (one unsigned per (batch, head),
+// rounded up to 256 bytes so the partials after them stay aligned).
+size_t decode_arrival_bytes(int64_t bh) {
+  return (static_cast<size_t>(bh) * sizeof(unsigned) + 255) & ~size_t(255);
+}
+
 // ------------------------------------------------------------------ driver entry point
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -280,11 +286,12 @@ TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, 
   const int64_t bh = batch * heads;
   const int chunk = decode_chunk(bh, kv_len);
   const int64_t n_chunks = (kv_len + chunk - 1) / chunk;
-  // Decode: the work counter, then (with more than one chunk) the FP32 partials.
+  // Decode: the work counter, then (with more than one chunk) the per-sequence arrival
+  // counters and the FP32 partials.
   size_t bytes = tt::decode::kCounterBytes;
   if (n_chunks > 1)
-    bytes += static_cast<size_t>(bh) * static_cast<size_t>(n_chunks) * tt::decode::PARTIAL *
-             sizeof(float);
+    bytes += decode_arrival_bytes(bh) + static_cast<size_t>(bh) * static_cast<size_t>(n_chunks) *
+                                            tt::decode::PARTIAL * sizeof(float);
   return bytes;
 }
 
@@ -675,40 +682,25 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     p.n_chunks = static_cast<int>(n_chunks);
     p.o = static_cast<__nv_bfloat16*>(out);
     p.lse = lse;
-    p.counter = static_cast<unsigned*>(workspace);
-    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                          tt::decode::kCounterBytes);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const size_t arrival_bytes = n_chunks > 1 ? decode_arrival_bytes(bh) : 0;
+    p.counter = reinterpret_cast<unsigned*>(ws);
+    p.arrivals = reinterpret_cast<unsigned*>(ws + tt::decode::kCounterBytes);
+    p.partials = reinterpret_cast<float*>(ws + tt::decode::kCounterBytes + arrival_bytes);
     p.scale_log2 = kScaleLog2;
-    // The CTAs take work items from a counter that must start at zero.
-    const cudaError_t me = cudaMemsetAsync(p.counter, 0, sizeof(unsigned), cs);
+    // The CTAs take work items from a counter, and count each split sequence's published
+    // partials, from zero: one memset clears both.
+    const size_t clear =
+        n_chunks > 1 ? tt::decode::kCounterBytes + arrival_bytes : sizeof(unsigned);
+    const cudaError_t me = cudaMemsetAsync(ws, 0, clear, cs);
     if (me != cudaSuccess)
-      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaMemsetAsync(work counter): ") +
+      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaMemsetAsync(decode counters): ") +
                                            cudaGetErrorString(me));
     // Persistent grid: one CTA per SM streams work items; no more CTAs than items.
     const int64_t ctas = std::min<int64_t>(sm_count, grid);
     tt::decode::decode_split_kernel<<<static_cast<unsigned>(ctas), tt::decode::THREADS,
                                       tt::decode::kSmemBytes, cs>>>(p);
-    if ((st = check_launch("decode_split_kernel launch")) != TT_ATTN_OK) return st;
-    if (n_chunks > 1) {
-      // Programmatic dependent launch: the combine grid may start while the split grid drains;
-      // it waits (griddepcontrol.wait) for the split grid's memory before reading partials.
-      cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3(static_cast<unsigned>((bh + tt::decode::COMBINE_WARPS - 1) /
-                                               tt::decode::COMBINE_WARPS));
-      cfg.blockDim = dim3(tt::decode::COMBINE_WARPS * 32);
-      cfg.dynamicSmemBytes = 0;
-      cfg.stream = cs;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[0].val.programmaticStreamSerializationAllowed = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      const cudaError_t le = cudaLaunchKernelEx(&cfg, tt::decode::decode_combine_kernel, p);
-      if (le != cudaSuccess)
-        return fail(TT_ATTN_LAUNCH_FAIL, std::string("decode_combine_kernel launch: ") +
-                                             cudaGetErrorString(le));
-    }
-    return TT_ATTN_OK;
+    return check_launch("decode_split_kernel launch");
   }
 
   CUtensorMap tmq, tmk, tmv;
@@ -787,7 +779,8 @@ TT_ATTN_API tt_attn_status tt_attn_decode_bf16_noalloc(
     }
     scratch = g_noalloc_scratch_ptr[dev];
   }
-  // The partials are written before they are read on every call, so nothing has to be cleared.
+  // Each call clears the counters it uses and writes every partial before it is read, so the
+  // scratch needs no clearing between calls.
   return tt_attn_forward_bf16(q, q_strides, k, k_strides, v, v_strides, batch, heads, 1, kv_len,
                               TT_ATTN_HEAD_DIM, kv_len - 1, kv_lens, out, lse, scratch,
                               kNoAllocScratchBytes, stream);
