@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 PREFILL_CFG = dict(B=4, H=12, T=4096, D=64)
 DECODE_CFG = dict(B=64, H=12, Tk=8192, D=64, len_lo=1024, len_hi=8192, seed=2026)
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+E2E_SLICES = 8  # (batch, head) row slices of the overlapped host-buffer e2e call
 
 
 def load_peaks():
@@ -203,6 +204,7 @@ def run_ours(args):
     import __graft_entry__
     __graft_entry__.import_package()
     from tiny_transformer_b200.operators import student
+    from tiny_transformer_b200.operators.host_stream import attention_from_host
     from tiny_transformer_b200.operators._extension import load_attention_extension
     from oracle import attention_oracle as oracle
     ext = load_attention_extension()
@@ -241,13 +243,19 @@ def run_ours(args):
         ho = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
         hl = torch.empty(q.shape[:-1], dtype=torch.float32, pin_memory=True)
 
-        def e2e():
+        def e2e_serial():
             dq, dk, dv = [h.to("cuda", non_blocking=True) for h in (hq, hk, hv)]
             o, lse = student.attention_with_lse(dq, dk, dv, 0)
             ho.copy_(o, non_blocking=True)
             hl.copy_(lse, non_blocking=True)
-        e2e_ms = sum(time_device(torch, e2e, max(3, args.steps // 2), 2)) / max(3, args.steps // 2)
-        e2e_ms = reduce_max(e2e_ms, world)
+
+        def e2e():
+            # The same copies and kernel, sliced by (batch, head) rows so that input copies,
+            # kernels and output copies overlap on three streams.
+            attention_from_host(hq, hk, hv, 0, out=ho, lse=hl, slices=E2E_SLICES)
+        e2e_steps = max(3, args.steps // 2)
+        e2e_ms = reduce_max(sum(time_device(torch, e2e, e2e_steps, 2)) / e2e_steps, world)
+        serial_ms = reduce_max(sum(time_device(torch, e2e_serial, e2e_steps, 2)) / e2e_steps, world)
         h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
         d2h = ho.numel() * 2 + hl.numel() * 4
         achieved = flops / (kernel_ms * 1e-3) / 1e12
@@ -268,7 +276,11 @@ def run_ours(args):
                          "traffic": tr, "algorithmic_flops": flops},
             "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h,
+                    "api": f"operators.host_stream.attention_from_host, {E2E_SLICES} slices",
+                    "serial": {"value": round(world * flops / (serial_ms * 1e-3) / 1e12, 3),
+                               "ms_per_step": round(serial_ms, 3),
+                               "api": "copy in, student.attention_with_lse, copy out"}},
             "gpu_launches": args.steps,
             "sdpa": {"value": round(flops / (sdpa_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                      "ms_per_step": round(sdpa_ms, 4)},
