@@ -3,21 +3,30 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
 
 Headline line (``--workload prefill``, default): BASELINE config 3, causal prefill
-B=4 H=12 Tq=Tk=4096 D=64 BF16 N(0,1), one step = one forward call; metric TFLOP/s over the
-visible (i, j) pairs (4*B*H*D*T(T+1)/2 FLOP). The same line carries a ``decode`` block for
-BASELINE config 4 (B=64 H=12 Tk=8192 decode, per-sequence lengths U[1024, 8192] by seed),
-metric GB/s of the visible K/V rows plus q, O and LSE. ``--workload decode`` prints the decode
-measurement as the headline instead; ``--workload generation`` times BASELINE config 5 (greedy
-generation through a random-init decoder, TTFT / TPOT / tokens per second per attention
-backend).
+B=4 H=12 Tq=Tk=4096 D=64 BF16 N(0,1), one step = one forward call over the whole workload;
+metric TFLOP/s over the visible (i, j) pairs (4*B*H*D*T(T+1)/2 FLOP). The same line carries
 
-Multi-GPU (torchrun, one process per GPU): each rank owns an independent shard of the same shape
-(weak scaling: the (batch x head) work of prefill and the batch of decode partition without any
-exchange), timing is the max over ranks, ``value`` is the whole-job aggregate.
+* ``decode``: BASELINE config 4 (B=64 H=12 Tk=8192 decode, per-sequence lengths U[1024, 8192]
+  by seed), GB/s of the visible K/V rows plus q, O and LSE;
+* ``backward``: dQ/dK/dV of config 3;
+* ``cfg1`` / ``cfg2``: the two shapes the reference publishes numbers for (prefill B=8 H=12
+  T=512; decode B=8 H=12 Tk=512), timed with the reference's CUDA-graph replay protocol
+  (tiny_transformer/benchmarks/linear_kernels.py:32-68: warmup 20, 100 calls per graph,
+  5 trials, median), torch SDPA beside each;
+* ``parity``: the outputs of the timed calls checked against the CPU oracle outside the
+  timed region (sampled rows of config 3 / 4, all of configs 1 / 2);
+* ``generation`` (one GPU only): BASELINE config 5, greedy generation through a random-init
+  decoder, TTFT / TPOT / tokens per second per attention backend.
 
-``--impl reference`` times the CPU oracle (a numpy restatement of the reference's
-``reference.attention``, oracle/attention_oracle.py) on the host cores on a bounded sample of the
-same workload; under torchrun only rank 0 runs it.
+Multi-GPU (torchrun, one process per GPU): strong scaling of the fixed workloads. Every rank
+builds the same config 3 / config 4 inputs and computes its shard - prefill and backward by
+(batch x head) rows, decode by batch rows balanced by visible keys (``sharding.py``); no
+collective runs in the timed region. Timing is the max over ranks; ``value`` is the whole
+workload's work divided by that time.
+
+``--impl reference`` times the reference's own CPU arithmetic (the ATen operations of
+``reference.attention``, oracle/torch_cpu_reference.py) on the host cores; under torchrun only
+rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -28,7 +37,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 import numpy as np
@@ -36,10 +44,16 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PREFILL_CFG = dict(B=4, H=12, T=4096, D=64)
-DECODE_CFG = dict(B=64, H=12, Tk=8192, D=64, len_lo=1024, len_hi=8192, seed=2026)
+PREFILL_CFG = dict(B=4, H=12, T=4096, D=64, seed=1000)
+DECODE_CFG = dict(B=64, H=12, Tk=8192, D=64, len_lo=1024, len_hi=8192, seed=2026, data_seed=2000)
+CFG1 = dict(B=8, H=12, T=512, D=64, seed=3000)
+CFG2 = dict(B=8, H=12, Tk=512, D=64, seed=3100)
+# The reference's operator-benchmark protocol (docs/performance.md:5, linear_kernels.py:51-68).
+GRAPH_PROTOCOL = dict(warmup=20, repeats=100, trials=5)
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 E2E_SLICES = 8  # (batch, head) row slices of the overlapped host-buffer e2e call
+# Acceptance bars of the north star, vs the reference's BF16 math path.
+PARITY_BARS = dict(max_abs=2e-2, mean_abs=2e-3, lse_rel=1e-3)
 
 
 def load_peaks():
@@ -140,6 +154,18 @@ def reduce_max(value, world):
     return float(t.item())
 
 
+def gather_values(value, world):
+    """Every rank's value, in rank order (one all_gather; [value] at world 1)."""
+    if world == 1:
+        return [value]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [round(float(x.item()), 4) for x in out]
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -147,27 +173,40 @@ def barrier(world):
 
 
 # ----------------------------------------------------------------------------- workloads
-def decode_lengths(cfg, rank):
-    rng = np.random.default_rng(cfg["seed"] + rank)
+def decode_lengths(cfg=DECODE_CFG):
+    rng = np.random.default_rng(cfg["seed"])
     return rng.integers(cfg["len_lo"], cfg["len_hi"] + 1, size=cfg["B"]).astype(np.int32)
 
 
-def make_prefill(torch, rank):
-    c = PREFILL_CFG
-    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    shape = (c["B"], c["H"], c["T"], c["D"])
-    q, k, v = [torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
-    return q, k, v
+def make_prefill(torch, cfg=PREFILL_CFG):
+    """Seeded N(0, 1) bf16 q, k, v of shape (B, H, T, 64) on the current CUDA device; the same
+    tensors on every rank (the whole workload; ranks take shards of it)."""
+    g = torch.Generator(device="cuda").manual_seed(cfg["seed"])
+    shape = (cfg["B"], cfg["H"], cfg["T"], cfg["D"])
+    return [torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
 
 
-def make_decode(torch, rank):
-    c = DECODE_CFG
-    g = torch.Generator(device="cuda").manual_seed(2000 + rank)
-    q = torch.randn((c["B"], c["H"], 1, c["D"]), generator=g, device="cuda", dtype=torch.bfloat16)
-    k = torch.randn((c["B"], c["H"], c["Tk"], c["D"]), generator=g, device="cuda", dtype=torch.bfloat16)
-    v = torch.randn_like(k)
-    lens = torch.from_numpy(decode_lengths(c, rank)).cuda()
+def make_decode(torch, cfg=DECODE_CFG, with_lens=True):
+    """Seeded q (B, H, 1, 64) and K/V caches (B, H, Tk, 64), plus the per-sequence lengths
+    (int32, on the device) drawn from cfg's length seed, or None."""
+    g = torch.Generator(device="cuda").manual_seed(cfg["data_seed"])
+    q = torch.randn((cfg["B"], cfg["H"], 1, cfg["D"]), generator=g, device="cuda",
+                    dtype=torch.bfloat16)
+    kv_shape = (cfg["B"], cfg["H"], cfg["Tk"], cfg["D"])
+    k = torch.randn(kv_shape, generator=g, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(kv_shape, generator=g, device="cuda", dtype=torch.bfloat16)
+    lens = torch.from_numpy(decode_lengths(cfg)).cuda() if with_lens else None
     return q, k, v, lens
+
+
+def prefill_shard(world, rank, cfg=PREFILL_CFG):
+    from tiny_transformer_b200.sharding import even_shards
+    return even_shards(cfg["B"] * cfg["H"], world)[rank]
+
+
+def decode_shard(world, rank, lens_np):
+    from tiny_transformer_b200.sharding import balanced_batch_shards
+    return balanced_batch_shards(lens_np.tolist(), world)[rank]
 
 
 def time_device(torch, fn, steps, warmup, flush=None):
@@ -192,6 +231,76 @@ def time_device(torch, fn, steps, warmup, flush=None):
     return times
 
 
+def time_graph(torch, fn, warmup, repeats, trials):
+    """The reference's graph protocol (linear_kernels.py:32-68, restated): `warmup` eager calls
+    on a side stream, `repeats` calls captured in one CUDA graph, one untimed replay, then
+    `trials` timed replays; returns (median us per call, per-trial us)."""
+    cur = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    side.wait_stream(cur)
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for _ in range(repeats):
+            fn()
+    with torch.cuda.stream(side):
+        graph.replay()
+    cur.wait_stream(side)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    samples = []
+    for _ in range(trials):
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        samples.append(a.elapsed_time(b) * 1000.0 / repeats)
+    del graph
+    return statistics.median(samples), [round(s, 3) for s in samples]
+
+
+# ----------------------------------------------------------------------------- parity (checker)
+def _parity_stats(out, lse, ref_bf16, ref_lse64):
+    diff = np.abs(np.asarray(out, np.float64) - np.asarray(ref_bf16, np.float64))
+    fin = np.isfinite(ref_lse64)
+    rel = (np.abs(np.asarray(lse, np.float64)[fin] - ref_lse64[fin])
+           / np.maximum(np.abs(ref_lse64[fin]), 1.0))
+    return float(diff.max()), float(diff.mean()), float(rel.max()) if rel.size else 0.0
+
+
+def parity_block(items, sample):
+    """Check (out, lse, q, k, v, past_len, kv_lens) items (host numpy float32) against the CPU
+    oracle: max / mean |dO| vs the BF16 reference restatement, LSE relative error vs FP64."""
+    from oracle import attention_oracle as oracle
+    mx, means, lr, n = 0.0, [], 0.0, 0
+    for out, lse, q, k, v, past_len, kv_lens in items:
+        if kv_lens is None:
+            ref_o = oracle.reference_attention_bf16(q, k, v, past_len)
+            _, ref_lse = oracle.attention_fp64(q, k, v, past_len)
+        else:
+            ref_o, _ = oracle.decode_with_kv_lens(q, k, v, kv_lens, oracle.reference_bf16_with_lse)
+            _, ref_lse = oracle.decode_with_kv_lens(q, k, v, kv_lens)
+        a, b, c = _parity_stats(out, lse, ref_o, ref_lse)
+        mx, lr = max(mx, a), max(lr, c)
+        means.append(b * out.size)
+        n += out.size
+    mean = sum(means) / max(n, 1)
+    ok = mx <= PARITY_BARS["max_abs"] and mean <= PARITY_BARS["mean_abs"] and \
+        lr <= PARITY_BARS["lse_rel"]
+    return {"max_abs": round(mx, 6), "mean_abs": round(mean, 7), "lse_rel": round(lr, 8),
+            "pass": bool(ok), "bars": PARITY_BARS, "sample": sample,
+            "oracle": "numpy restatement of reference.attention (bf16) and FP64 LSE"}
+
+
+def _host(x):
+    return x.detach().float().cpu().numpy()
+
+
+# ----------------------------------------------------------------------------- our arm
 def run_ours(args):
     import torch
     world, rank, local = init_dist()
@@ -206,6 +315,7 @@ def run_ours(args):
     from tiny_transformer_b200.operators import student
     from tiny_transformer_b200.operators.host_stream import attention_from_host
     from tiny_transformer_b200.operators._extension import load_attention_extension
+    from tiny_transformer_b200.sharding import prefill_slice
     from oracle import attention_oracle as oracle
     ext = load_attention_extension()
     peaks = load_peaks()
@@ -224,8 +334,11 @@ def run_ours(args):
     with torch.no_grad():
         # ------------------------------------------------------------------ prefill (cfg 3)
         c = PREFILL_CFG
-        q, k, v = make_prefill(torch, rank)
-        flops = oracle.prefill_flops(c["B"], c["H"], c["T"], c["T"], 0)
+        q_all, k_all, v_all = make_prefill(torch)
+        shard = prefill_shard(world, rank)
+        q, k, v = (prefill_slice(x, shard) for x in (q_all, k_all, v_all))
+        flops_total = oracle.prefill_flops(c["B"], c["H"], c["T"], c["T"], 0)
+        flops_rank = oracle.prefill_flops(shard.size, 1, c["T"], c["T"], 0)
         fn = lambda: ext.attention_forward(q, k, v, 0)  # noqa: E731
         barrier(world)
         torch.cuda.synchronize()
@@ -235,10 +348,12 @@ def run_ours(args):
             torch.cuda.synchronize()
         kernel_ms = sum(times) / len(times)
         step_ms = reduce_max(kernel_ms, world)
-        # SDPA (FlashAttention backend) on the same GPU and inputs, for context.
+        per_rank_ms = gather_values(kernel_ms, world)
+        # SDPA (cuDNN / FlashAttention backend) on the same GPU and shard, for context.
         sd = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)  # noqa: E731
-        sdpa_ms = sum(time_device(torch, sd, max(3, args.steps // 2), args.warmup, flush)) / max(3, args.steps // 2)
-        # end to end through the public operator: pinned host -> device, call, device -> host
+        n_sd = max(3, args.steps // 2)
+        sdpa_ms = reduce_max(sum(time_device(torch, sd, n_sd, args.warmup, flush)) / n_sd, world)
+        # End to end through the public operator: pinned host -> device, call, device -> host.
         hq, hk, hv = [x.cpu().pin_memory() for x in (q, k, v)]
         ho = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
         hl = torch.empty(q.shape[:-1], dtype=torch.float32, pin_memory=True)
@@ -258,43 +373,58 @@ def run_ours(args):
         serial_ms = reduce_max(sum(time_device(torch, e2e_serial, e2e_steps, 2)) / e2e_steps, world)
         h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
         d2h = ho.numel() * 2 + hl.numel() * 4
-        achieved = flops / (kernel_ms * 1e-3) / 1e12
+        achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
         tr = traffic.get("attention_prefill_kernel")
+        # Parity of the timed call's outputs (outside every timed region): the first and the
+        # last (batch, head) row of this rank's shard against the CPU oracle.
+        out, lse = fn()
+        rows = sorted({0, shard.size - 1})
+        par = parity_block(
+            [(_host(out[r:r + 1]), _host(lse[r:r + 1]), _host(q[r:r + 1]), _host(k[r:r + 1]),
+              _host(v[r:r + 1]), 0, None) for r in rows],
+            f"(batch x head) rows {[shard.start + r for r in rows]} of cfg3 (T=4096), rank {rank}")
         results["prefill"] = {
             "metric": "causal attn fwd TFLOP/s (prefill)",
-            "value": round(world * flops / (step_ms * 1e-3) / 1e12, 2),
+            "value": round(flops_total / (step_ms * 1e-3) / 1e12, 2),
             "unit": "TFLOP/s",
             "ms_per_step": round(step_ms, 4),
-            "config": {"workload": "cfg3 causal prefill B=4 H=12 Tq=Tk=4096 D=64 bf16 N(0,1), per rank",
-                       "global_batch": c["B"] * world, "heads": c["H"], "seq_len": c["T"],
-                       "head_dim": c["D"], "parallelism": f"(batch x head) shards, {world} rank(s)",
+            "config": {"workload": "cfg3 causal prefill B=4 H=12 Tq=Tk=4096 D=64 bf16 N(0,1), "
+                                   "whole workload split over the ranks",
+                       "global_batch": c["B"], "heads": c["H"], "seq_len": c["T"],
+                       "head_dim": c["D"],
+                       "parallelism": f"dp{world}: (batch x head) rows {c['B'] * c['H']} split "
+                                      f"{[prefill_shard(world, r).size for r in range(world)]}",
                        "l2": "flushed between timed steps (256 MiB write)"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops"], 4),
                          "peak_kind": f"{peaks['source']} burst cuBLAS bf16",
-                         "traffic": tr, "algorithmic_flops": flops},
-            "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
+                         "traffic": (tr * shard.size / (c["B"] * c["H"])) if tr else None,
+                         "algorithmic_flops": flops_rank},
+            "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world,
                     "api": f"operators.host_stream.attention_from_host, {E2E_SLICES} slices",
-                    "serial": {"value": round(world * flops / (serial_ms * 1e-3) / 1e12, 3),
+                    "serial": {"value": round(flops_total / (serial_ms * 1e-3) / 1e12, 3),
                                "ms_per_step": round(serial_ms, 3),
                                "api": "copy in, student.attention_with_lse, copy out"}},
             "gpu_launches": args.steps,
-            "sdpa": {"value": round(flops / (sdpa_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "per_rank_ms": per_rank_ms,
+            "sdpa": {"value": round(flops_total / (sdpa_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                      "ms_per_step": round(sdpa_ms, 4)},
+            "parity": par,
             "clocks": clk.summary(),
         }
-        del hq, hk, hv, ho, hl
+        del hq, hk, hv, ho, hl, out, lse
 
         # ------------------------------------------------------------------ backward (cfg 3)
-        # dQ, dK, dV of the same prefill (the training path of student.attention); work counted
-        # as 2.5x the forward FLOPs (five GEMMs: QK^T recomputed, dO.V^T, P^T.dO, dS^T.Q, dS.K).
+        # dQ, dK, dV of the same prefill shard (the training path of student.attention); work
+        # counted as 2.5x the forward FLOPs (five GEMMs: QK^T recomputed, dO.V^T, P^T.dO,
+        # dS^T.Q, dS.K).
         out, lse = ext.attention_forward(q, k, v, 0)
-        g = torch.Generator(device="cuda").manual_seed(77 + rank)
-        dout = torch.randn(q.shape, device="cuda", dtype=torch.bfloat16, generator=g)
-        bwd_flops = 2.5 * flops
+        g = torch.Generator(device="cuda").manual_seed(77)
+        dout_all = torch.randn(q_all.shape, device="cuda", dtype=torch.bfloat16, generator=g)
+        dout = prefill_slice(dout_all, shard)
         bsteps = max(3, args.steps // 2)
         fn = lambda: ext.attention_backward(q, k, v, dout, out, lse, 0)  # noqa: E731
         barrier(world)
@@ -303,49 +433,59 @@ def run_ours(args):
         barrier(world)
         torch.cuda.synchronize()
         bwd_ms = reduce_max(sum(times) / len(times), world)
-        # The fixed-order path taken under torch.use_deterministic_algorithms(True) (this rank).
+        bwd_rank_ms = sum(times) / len(times)
+        # The fixed-order path taken under torch.use_deterministic_algorithms(True).
         det_mode = (torch.are_deterministic_algorithms_enabled(),
                     torch.is_deterministic_algorithms_warn_only_enabled())
         torch.use_deterministic_algorithms(True)
         try:
-            det_ms = sum(time_device(torch, fn, bsteps, args.warmup, flush)) / bsteps
+            det_ms = reduce_max(sum(time_device(torch, fn, bsteps, args.warmup, flush)) / bsteps,
+                                world)
         finally:
             torch.use_deterministic_algorithms(det_mode[0], warn_only=det_mode[1])
         with torch.enable_grad():
             qq, kk, vv = [x.detach().requires_grad_() for x in (q, k, v)]
             o2 = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True)
             sd = lambda: torch.autograd.grad(o2, (qq, kk, vv), dout, retain_graph=True)  # noqa: E731
-            sdpa_bwd_ms = sum(time_device(torch, sd, bsteps, args.warmup, flush)) / bsteps
+            sdpa_bwd_ms = reduce_max(sum(time_device(torch, sd, bsteps, args.warmup, flush)) / bsteps,
+                                     world)
             del qq, kk, vv, o2
+        bwd_flops = 2.5 * flops_total
         results["backward"] = {
             "metric": "causal attn bwd TFLOP/s (2.5x forward FLOPs)",
-            "value": round(world * bwd_flops / (bwd_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "value": round(bwd_flops / (bwd_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
             "ms_per_step": round(bwd_ms, 4),
             "config": {"workload": "cfg3 backward (dQ, dK, dV) B=4 H=12 Tq=Tk=4096 D=64 bf16, "
-                                   "per rank", "algorithmic_flops": bwd_flops},
+                                   "whole workload split over the ranks",
+                       "algorithmic_flops": bwd_flops},
             "roofline": {"bound": "tensor",
-                         "achieved": round(bwd_flops / (bwd_ms * 1e-3) / 1e12, 2),
+                         "achieved": round(2.5 * flops_rank / (bwd_rank_ms * 1e-3) / 1e12, 2),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": round(bwd_flops / (bwd_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)},
+                         "frac": round(2.5 * flops_rank / (bwd_rank_ms * 1e-3) / 1e12
+                                       / peaks["bf16_tflops"], 4)},
             "gpu_launches": 3 * bsteps,
             "sdpa": {"value": round(bwd_flops / (sdpa_bwd_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                      "ms_per_step": round(sdpa_bwd_ms, 4)},
             "deterministic": {"value": round(bwd_flops / (det_ms * 1e-3) / 1e12, 2),
                               "unit": "TFLOP/s", "ms_per_step": round(det_ms, 4)},
         }
-        del q, k, v, out, lse, dout
+        del q, k, v, out, lse, dout, dout_all, q_all, k_all, v_all
 
         # ------------------------------------------------------------------ decode (cfg 4)
         c = DECODE_CFG
-        q, k, v, lens = make_decode(torch, rank)
-        lens_np = lens.cpu().numpy()
-        nbytes = oracle.decode_bytes(c["B"], c["H"], lens_np)
+        q_all, k_all, v_all, lens_all = make_decode(torch)
+        lens_np = decode_lengths()
+        dsh = decode_shard(world, rank, lens_np)
+        sl = slice(dsh.start, dsh.stop)
+        q, k, v, lens = q_all[sl], k_all[sl], v_all[sl], lens_all[sl]
+        nbytes_total = oracle.decode_bytes(c["B"], c["H"], lens_np)
+        nbytes_rank = oracle.decode_bytes(dsh.size, c["H"], lens_np[sl])
         fn = lambda: ext.attention_forward(q, k, v, c["Tk"] - 1, None, lens)  # noqa: E731
         barrier(world)
         torch.cuda.synchronize()
-        # The K/V read (~0.9 GB) is 7x L2, so the headline uses no flush: a 256 MiB flush write
-        # leaves up to L2's worth of dirty lines whose write-back would land inside the timed
-        # step. The flushed timing is reported beside it.
+        # The K/V read (~0.9 GB at one GPU) is 7x L2, so the headline uses no flush: a 256 MiB
+        # flush write leaves up to L2's worth of dirty lines whose write-back would land inside
+        # the timed step. The flushed timing is reported beside it.
         with ClockSampler(local) as clk:
             times = time_device(torch, fn, args.steps, args.warmup, busy)
             flushed = time_device(torch, fn, args.steps, args.warmup, flush)
@@ -353,6 +493,7 @@ def run_ours(args):
             torch.cuda.synchronize()
         kernel_ms = sum(times) / len(times)
         step_ms = reduce_max(kernel_ms, world)
+        per_rank_ms = gather_values(kernel_ms, world)
         flushed_ms = reduce_max(sum(flushed) / len(flushed), world)
         # e2e: the cache lives on the device (it is the model's KV cache); per step the host
         # sends q and the lengths and reads back O and LSE.
@@ -367,152 +508,279 @@ def run_ours(args):
             o, lse = student.attention_with_lse(dq, k, v, c["Tk"] - 1, None, dl)
             ho.copy_(o, non_blocking=True)
             hl.copy_(lse, non_blocking=True)
-        e2e_ms = sum(time_device(torch, e2e, max(3, args.steps // 2), 2)) / max(3, args.steps // 2)
-        e2e_ms = reduce_max(e2e_ms, world)
-        achieved = nbytes / (kernel_ms * 1e-3) / 1e9
+        n_e2e = max(3, args.steps // 2)
+        e2e_ms = reduce_max(sum(time_device(torch, e2e, n_e2e, 2)) / n_e2e, world)
+        achieved = nbytes_rank / (kernel_ms * 1e-3) / 1e9
         tr = traffic.get("decode_split_kernel")
+        out, lse = fn()
+        rows = sorted({0, dsh.size // 2, dsh.size - 1})
+        items = []
+        for r in rows:
+            L = int(lens_np[dsh.start + r])
+            items.append((_host(out[r:r + 1]), _host(lse[r:r + 1]), _host(q[r:r + 1]),
+                          _host(k[r:r + 1, :, :L]), _host(v[r:r + 1, :, :L]), L - 1, None))
+        par = parity_block(items, f"sequences {[dsh.start + r for r in rows]} of cfg4, rank {rank}")
         results["decode"] = {
             "metric": "decode KV GB/s",
-            "value": round(world * nbytes / (step_ms * 1e-3) / 1e9, 1),
+            "value": round(nbytes_total / (step_ms * 1e-3) / 1e9, 1),
             "unit": "GB/s",
             "ms_per_step": round(step_ms, 4),
             "config": {"workload": "cfg4 decode B=64 H=12 Tk=8192 D=64 bf16, kv_lens U[1024,8192] "
-                                   f"seed {c['seed']}+rank, per rank",
-                       "global_batch": c["B"] * world, "heads": c["H"], "kv_capacity": c["Tk"],
-                       "sum_kv_lens_rank0": int(lens_np.sum()), "algorithmic_bytes": nbytes,
-                       "parallelism": f"batch shards, {world} rank(s)",
-                       "l2": "inputs larger than L2 (K/V read ~0.9 GB, 7x L2), no flush; a "
-                             "spin kernel ahead of each step keeps host latency out"},
+                                   f"seed {c['seed']}, whole workload split over the ranks",
+                       "global_batch": c["B"], "heads": c["H"], "kv_capacity": c["Tk"],
+                       "sum_kv_lens": int(lens_np.sum()), "algorithmic_bytes": nbytes_total,
+                       "parallelism": f"dp{world}: batch rows split by visible keys "
+                                      f"{[decode_shard(world, r, lens_np).size for r in range(world)]}",
+                       "l2": "inputs larger than L2 (K/V read ~0.9 GB at 1 GPU, 7x L2), no "
+                             "flush; a spin kernel ahead of each step keeps host latency out"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "peak_kind": f"{peaks['source']} copy bandwidth", "traffic": tr,
-                         "algorithmic_bytes": nbytes},
-            "e2e": {"value": round(world * nbytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                         "peak_kind": f"{peaks['source']} copy bandwidth",
+                         "traffic": (tr * nbytes_rank / nbytes_total) if tr else None,
+                         "algorithmic_bytes": nbytes_rank},
+            "e2e": {"value": round(nbytes_total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": hq.numel() * 2 + hlens.numel() * 4,
-                    "d2h_bytes_per_step": ho.numel() * 2 + hl.numel() * 4},
+                    "h2d_bytes_per_step": (hq.numel() * 2 + hlens.numel() * 4) * world,
+                    "d2h_bytes_per_step": (ho.numel() * 2 + hl.numel() * 4) * world},
             "gpu_launches": args.steps,
-            "flushed": {"value": round(world * nbytes / (flushed_ms * 1e-3) / 1e9, 1),
+            "per_rank_ms": per_rank_ms,
+            "flushed": {"value": round(nbytes_total / (flushed_ms * 1e-3) / 1e9, 1),
                         "ms_per_step": round(flushed_ms, 4),
                         "l2": "256 MiB write between timed steps"},
+            "parity": par,
             "clocks": clk.summary(),
         }
+        del q, k, v, lens, q_all, k_all, v_all, lens_all, out, lse, hq, hlens, ho, hl
 
+        # ------------------------------------------------------------------ cfg1 / cfg2
+        # The reference's own published shapes, each whole on every rank (latency-bound; not
+        # sharded), timed with the reference's CUDA-graph replay protocol.
+        results["cfg1"] = small_case(torch, ext, oracle, "prefill", peaks)
+        results["cfg2"] = small_case(torch, ext, oracle, "decode", peaks)
+
+    if world == 1 and not args.no_generation:
+        results["generation"] = generation_block(max(1, min(args.steps, 3)))
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
     if rank != 0:
         return
     head_key = "decode" if args.workload == "decode" else "prefill"
-    other_key = "prefill" if head_key == "decode" else "decode"
     head = results[head_key]
     line = {
         "metric": head["metric"], "value": head["value"], "unit": head["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic N(0,1), seeded", "impl": "ours", "config": head["config"],
         "roofline": head["roofline"], "e2e": head["e2e"], "gpu_launches": head["gpu_launches"],
         "clocks": head["clocks"],
         "cpu_baseline": cpu_baseline(head_key, budget_s=args.cpu_budget) if world == 1 else None,
     }
-    if "sdpa" in head:
-        line["sdpa"] = head["sdpa"]
-    line[other_key] = results[other_key]
-    line["backward"] = results["backward"]
+    for key in ("sdpa", "per_rank_ms", "parity"):
+        if key in head:
+            line[key] = head[key]
+    for key, block in results.items():
+        if key != head_key:
+            line[key] = block
     print(json.dumps(line), flush=True)
 
 
+def small_case(torch, ext, oracle, kind, peaks):
+    """cfg1 (prefill B=8 H=12 T=512) or cfg2 (decode B=8 H=12 Tk=512): our operator and torch
+    SDPA, each timed by graph replay (GRAPH_PROTOCOL); parity of all outputs vs the oracle."""
+    P = GRAPH_PROTOCOL
+    if kind == "prefill":
+        c = CFG1
+        q, k, v = make_prefill(torch, c)
+        past = 0
+        work = oracle.prefill_flops(c["B"], c["H"], c["T"], c["T"], 0)
+        sd = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)  # noqa: E731
+        published = {"student_us": 39.78, "sdpa_us": 39.35, "hardware": "A100 80GB PCIe",
+                     "source": "reference README.md:26, docs/performance.md:9"}
+        shape = f"B={c['B']} H={c['H']} Tq=Tk={c['T']} D=64 causal"
+    else:
+        c = CFG2
+        q, k, v, _ = make_decode(torch, dict(c, data_seed=c["seed"]), with_lens=False)
+        past = c["Tk"] - 1
+        work = oracle.decode_bytes(c["B"], c["H"], [c["Tk"]] * c["B"])
+        # reference.sdpa_attention for one query row: no mask (reference.py:60-61).
+        sd = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=False)  # noqa: E731
+        published = {"student_us": 12.73, "sdpa_us": 15.44, "hardware": "A100 80GB PCIe",
+                     "source": "reference README.md:27, docs/performance.md:10"}
+        shape = f"B={c['B']} H={c['H']} Tq=1 Tk={c['Tk']} D=64 decode"
+    fn = lambda: ext.attention_forward(q, k, v, past)  # noqa: E731
+    us, trials = time_graph(torch, fn, P["warmup"], P["repeats"], P["trials"])
+    sdpa_us, _ = time_graph(torch, sd, P["warmup"], P["repeats"], P["trials"])
+    out, lse = fn()
+    par = parity_block([(_host(out), _host(lse), _host(q), _host(k), _host(v), past, None)],
+                       "all outputs")
+    if kind == "prefill":
+        rate = {"tflops": round(work / (us * 1e-6) / 1e12, 2),
+                "frac": round(work / (us * 1e-6) / 1e12 / peaks["bf16_tflops"], 4),
+                "sdpa_tflops": round(work / (sdpa_us * 1e-6) / 1e12, 2), "algorithmic_flops": work}
+    else:
+        rate = {"gbs": round(work / (us * 1e-6) / 1e9, 1),
+                "frac": round(work / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+                "sdpa_gbs": round(work / (sdpa_us * 1e-6) / 1e9, 1), "algorithmic_bytes": work}
+    return {"workload": f"cfg{1 if kind == 'prefill' else 2} {shape} bf16 N(0,1), whole on each rank",
+            "us": round(us, 3), "trials_us": trials, "sdpa_us": round(sdpa_us, 3), **rate,
+            "timing": "CUDA-graph replay, warmup 20, 100 calls per graph, 5 trials, median "
+                      "(inputs resident in L2, no flush, as the reference's protocol)",
+            "reference_published": published, "parity": par}
+
+
+def generation_block(repeats):
+    """BASELINE config 5 per attention backend (see run_generation); rank 0 / one GPU."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.import_package()
+    from tiny_transformer_b200.generation import Decoder, DecoderConfig, request
+
+    torch.manual_seed(GEN_CFG["seed"])
+    model = Decoder(DecoderConfig(), "student").to(device="cuda", dtype=torch.bfloat16).eval()
+    g = torch.Generator(device="cuda").manual_seed(GEN_CFG["seed"])
+    prompt = torch.randint(0, model.config.vocab_size, (GEN_CFG["batch"], GEN_CFG["prompt"]),
+                           device="cuda", generator=g)
+    results = {}
+    for name, backend, graphed in (("student_graphed", "student", True),
+                                   ("student", "student", False), ("sdpa", "sdpa", False),
+                                   ("reference", "reference", False)):
+        model.set_attention(backend)
+        request(model, prompt, GEN_CFG["new_tokens"], graphed=graphed)  # warm-up
+        trials = [request(model, prompt, GEN_CFG["new_tokens"], graphed=graphed)
+                  for _ in range(repeats)]
+        results[name] = {k: round(statistics.median(t[k] for t in trials), 4)
+                         for k in ("ttft_ms", "tpot_ms", "request_ms",
+                                   "output_tokens_per_second", "decode_tokens_per_second")}
+    del model
+    torch.cuda.empty_cache()
+    return {"workload": "cfg5 greedy generation, model_60m shape (8 layers, dim 768, 12 x 64 "
+                        "heads, SwiGLU 2048, vocab 8192, tied), random-init bf16 N(0, 0.02) "
+                        "weights, batch 32, prompt 128 ids uniform in [0, 8192), 256 new tokens",
+            "timing": f"host wall time around synchronisations, median of {repeats} requests "
+                      "after one warm-up (benchmarks/model.py:20-37)",
+            "kv_capacity": GEN_CFG["prompt"] + GEN_CFG["new_tokens"], "backends": results}
+
+
 # ----------------------------------------------------------------------------- CPU side
-def _cpu_workers():
-    """Host threads for the CPU oracle: all cores available to this process, capped at 32 so
-    the per-thread score matrices (~0.3 GB each at T=4096) stay well inside host memory."""
-    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    return max(1, min(int(n or 1), 32))
+def _cpu_prefill_inputs(torch, n_rows, seed=99):
+    g = torch.Generator().manual_seed(seed)
+    shape = (1, n_rows, PREFILL_CFG["T"], 64)
+    return [torch.randn(shape, generator=g).to(torch.bfloat16) for _ in range(3)]
 
 
-def cpu_sample(workload, n_items, rank_seed=0):
-    """Run the oracle port on `n_items` units of the workload in a thread pool (one unit per
-    thread, BLAS limited to one thread each). Returns (seconds, algorithmic units done)."""
-    from concurrent.futures import ThreadPoolExecutor
+def _cpu_decode_inputs(torch, n_seq, seed=99):
+    c = DECODE_CFG
+    lens = decode_lengths()
+    g = torch.Generator().manual_seed(seed)
+    items = []
+    for i in range(n_seq):
+        L = int(lens[i % len(lens)])
+        items.append(([torch.randn((1, c["H"], n, 64), generator=g).to(torch.bfloat16)
+                       for n in (1, L, L)], L))
+    return items
 
-    from threadpoolctl import threadpool_limits
+
+def cpu_baseline(workload, budget_s=12.0):
+    """The reference's ATen path (oracle/torch_cpu_reference.py) on all host cores, repeated on
+    samples of the workload until ``budget_s`` seconds of CPU work."""
+    import torch
 
     from oracle import attention_oracle as oracle
-    rng = np.random.default_rng(99 + rank_seed)
+    from oracle import torch_cpu_reference as tref
+    cores = tref.host_threads()
+    torch.set_num_threads(cores)
+    T = PREFILL_CFG["T"]
+    done, t_total, units = 0.0, 0.0, 0
+    t_start = time.perf_counter()
     if workload == "prefill":
-        T = PREFILL_CFG["T"]
-        items = [[oracle.round_bf16(rng.standard_normal((1, 1, T, 64), dtype=np.float32))
-                  for _ in range(3)] for _ in range(n_items)]
-        work = lambda it: oracle.reference_attention_bf16(*it, 0, return_lse=True)  # noqa: E731
-        unit = oracle.prefill_flops(1, 1, T, T, 0)
+        q, k, v = _cpu_prefill_inputs(torch, 4)
+        tref.prefill_rows(q, k, v, 0)  # warm-up
+        while units == 0 or time.perf_counter() - t_start < budget_s:
+            t0 = time.perf_counter()
+            tref.prefill_rows(q, k, v, 0)
+            t_total += time.perf_counter() - t0
+            done += oracle.prefill_flops(1, 4, T, T, 0)
+            units += 4
+        value, unit = done / t_total / 1e12, "TFLOP/s"
+        sample = (f"{units} (batch, head) rows of cfg3 (Tq=Tk=4096, causal), 4 rows per call, "
+                  f"torch ATen reference.attention on {cores} threads, {t_total:.1f} s")
     else:
-        c = DECODE_CFG
-        lens = decode_lengths(c, 0)
-        items = []
-        for i in range(n_items):
-            L = int(lens[i % len(lens)])
-            items.append(([oracle.round_bf16(rng.standard_normal((1, c["H"], 1, 64), dtype=np.float32))]
-                          + [oracle.round_bf16(rng.standard_normal((1, c["H"], L, 64), dtype=np.float32))
-                             for _ in range(2)], L))
-        work = lambda it: oracle.reference_attention_bf16(*it[0], it[1] - 1, return_lse=True)  # noqa: E731
-        unit = None
-    with threadpool_limits(limits=1):
-        t0 = time.perf_counter()
-        with ThreadPoolExecutor(max_workers=_cpu_workers()) as pool:
-            list(pool.map(work, items))
-        dt = time.perf_counter() - t0
-    if workload == "prefill":
-        done = unit * n_items
-    else:
-        done = sum(oracle.decode_bytes(1, DECODE_CFG["H"], [it[1]]) for it in items)
-    return dt, done
-
-
-def cpu_baseline(workload, budget_s=20.0):
-    cores = _cpu_workers()
-    if workload == "prefill":
-        dt, flops = cpu_sample("prefill", cores)
-        value, unit = flops / dt / 1e12, "TFLOP/s"
-        sample = (f"{cores} (batch, head) slices of cfg3 (Tq=Tk=4096, causal), one per thread, "
-                  f"numpy oracle port, {dt:.1f} s")
-    else:
-        n = cores * 4
-        dt, nbytes = cpu_sample("decode", n)
-        value, unit = nbytes / dt / 1e9, "GB/s"
-        sample = f"{n} sequences of cfg4 (12 heads, lengths from the cfg4 seed), numpy oracle port, {dt:.1f} s"
-    return {"value": round(value, 5), "unit": unit, "cores": cores, "kind": "port", "sample": sample}
+        items = _cpu_decode_inputs(torch, 16)
+        while units == 0 or time.perf_counter() - t_start < budget_s:
+            for (qq, kk, vv), L in items:
+                t0 = time.perf_counter()
+                tref.attention(qq, kk, vv, L - 1)
+                t_total += time.perf_counter() - t0
+                done += oracle.decode_bytes(1, DECODE_CFG["H"], [L])
+                units += 1
+        value, unit = done / t_total / 1e9, "GB/s"
+        sample = (f"{units} sequences of cfg4 (12 heads, lengths from the cfg4 seed), torch ATen "
+                  f"reference.attention on {cores} threads, {t_total:.1f} s")
+    return {"value": round(value, 5), "unit": unit, "cores": cores, "kind": "port",
+            "sample": sample}
 
 
 def run_reference(args):
+    """The reference arm: the reference's ATen arithmetic on the host CPU (all cores), on the
+    config-3 workload (or config 4 with ``--workload decode``). Each step covers the whole
+    workload when one step takes at most ``--cpu-step-budget`` seconds, otherwise a fixed sample
+    of its (batch, head) rows / sequences, stated in the line."""
     world, rank, _ = init_dist()
     if rank != 0:
         return
+    import torch
+
+    from oracle import attention_oracle as oracle
+    from oracle import torch_cpu_reference as tref
+    cores = tref.host_threads()
+    torch.set_num_threads(cores)
     workload = "decode" if args.workload == "decode" else "prefill"
-    cores = _cpu_workers()
-    times, done_total = [], 0
+    if workload == "prefill":
+        c = PREFILL_CFG
+        n_all = c["B"] * c["H"]
+        q, k, v = _cpu_prefill_inputs(torch, n_all, seed=c["seed"])
+        t0 = time.perf_counter()
+        tref.prefill_rows(q[:, :4], k[:, :4], v[:, :4], 0)
+        per_row = (time.perf_counter() - t0) / 4
+        n_rows = int(min(n_all, max(4, args.cpu_step_budget // max(per_row, 1e-9))))
+        n_rows -= n_rows % 4 if n_rows > 4 else 0
+        step = lambda: tref.prefill_rows(q[:, :n_rows], k[:, :n_rows], v[:, :n_rows], 0)  # noqa: E731
+        unit_work = oracle.prefill_flops(1, n_rows, c["T"], c["T"], 0)
+        metric, unit, scale = "causal attn fwd TFLOP/s (prefill)", "TFLOP/s", 1e12
+        cfg = {"workload": "cfg3 causal prefill B=4 H=12 Tq=Tk=4096 D=64 bf16 N(0,1)",
+               "sample_per_step": f"{n_rows} of {n_all} (batch, head) rows",
+               "same_config": n_rows == n_all}
+    else:
+        c = DECODE_CFG
+        items = _cpu_decode_inputs(torch, c["B"], seed=c["data_seed"])
+        lens = [L for _, L in items]
+
+        def step():
+            for (qq, kk, vv), L in items:
+                tref.attention(qq, kk, vv, L - 1)
+        unit_work = oracle.decode_bytes(c["B"], c["H"], lens)
+        metric, unit, scale = "decode KV GB/s", "GB/s", 1e9
+        cfg = {"workload": "cfg4 decode B=64 H=12 Tk=8192 D=64 bf16, kv_lens U[1024,8192]",
+               "sample_per_step": "all 64 sequences", "same_config": True}
+    times = []
     for i in range(args.warmup + args.steps):
-        n = cores if workload == "prefill" else cores * 4
-        dt, done = cpu_sample(workload, n, rank_seed=i)
+        t0 = time.perf_counter()
+        step()
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
             times.append(dt)
-            done_total += done
     total = sum(times)
-    if workload == "prefill":
-        value, unit, metric = done_total / total / 1e12, "TFLOP/s", "causal attn fwd TFLOP/s (prefill)"
-        cfg = {"workload": "cfg3 causal prefill B=4 H=12 Tq=Tk=4096 D=64 bf16 N(0,1)",
-               "sample_per_step": f"{cores} (batch, head) slices"}
-    else:
-        value, unit, metric = done_total / total / 1e9, "GB/s", "decode KV GB/s"
-        cfg = {"workload": "cfg4 decode B=64 H=12 Tk=8192 D=64 bf16, kv_lens U[1024,8192]",
-               "sample_per_step": f"{cores * 4} sequences"}
+    value = unit_work * len(times) / total / scale
     line = {
         "metric": metric, "value": round(value, 5), "unit": unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(times), 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic N(0,1), seeded", "impl": "reference", "config": cfg,
         "cpu_baseline": {"value": round(value, 5), "unit": unit, "cores": cores, "kind": "port",
-                         "sample": f"{cfg['sample_per_step']} per step, numpy restatement of "
-                                   "reference.attention (oracle/attention_oracle.py)"},
+                         "sample": f"{cfg['sample_per_step']} per step; the ATen operations of "
+                                   "reference.attention (reference.py:49-53) on CPU tensors, "
+                                   "oracle/torch_cpu_reference.py"},
         "e2e": {"value": round(value, 5), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -532,42 +800,19 @@ def run_generation(args):
     place), student graphed (one CUDA graph per decode step over the full-capacity cache with
     device-held kv_lens), torch SDPA and the reference specification. One GPU; under torchrun
     only rank 0 runs."""
-    import statistics
-
-    import torch
-    import __graft_entry__
-    __graft_entry__.import_package()
-    from tiny_transformer_b200.generation import Decoder, DecoderConfig, request
-
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    torch.manual_seed(GEN_CFG["seed"])
-    model = Decoder(DecoderConfig(), "student").to(device="cuda", dtype=torch.bfloat16).eval()
-    g = torch.Generator(device="cuda").manual_seed(GEN_CFG["seed"])
-    prompt = torch.randint(0, model.config.vocab_size, (GEN_CFG["batch"], GEN_CFG["prompt"]),
-                           device="cuda", generator=g)
     repeats = max(1, min(args.steps, 5))
-    results = {}
-    for name, backend, graphed in (("student_graphed", "student", True),
-                                   ("student", "student", False), ("sdpa", "sdpa", False),
-                                   ("reference", "reference", False)):
-        model.set_attention(backend)
-        request(model, prompt, GEN_CFG["new_tokens"], graphed=graphed)  # warm-up
-        trials = [request(model, prompt, GEN_CFG["new_tokens"], graphed=graphed)
-                  for _ in range(repeats)]
-        results[name] = {k: round(statistics.median(t[k] for t in trials), 4)
-                         for k in ("ttft_ms", "tpot_ms", "request_ms",
-                                   "output_tokens_per_second", "decode_tokens_per_second")}
-    head = results["student_graphed"]
+    block = generation_block(repeats)
+    head = block["backends"]["student_graphed"]
     line = {
         "metric": "decode_tokens_per_second", "value": head["decode_tokens_per_second"],
         "unit": "tokens/s", "n_gpus": 1, "steps": repeats, "warmup": 1,
         "ms_per_step": head["request_ms"], "higher_is_better": True, "scaling": "none",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic ids, random-init weights",
-        "config": {"workload": "cfg5 greedy generation, model_60m shape, batch 32, prompt 128, "
-                               "256 new tokens, attention=student (graphed decode)",
-                   "kv_capacity": GEN_CFG["prompt"] + GEN_CFG["new_tokens"]},
-        "backends": results,
+        "config": {"workload": block["workload"] + ", attention=student (graphed decode)",
+                   "kv_capacity": block["kv_capacity"]},
+        "backends": block["backends"],
     }
     print(json.dumps(line), flush=True)
 
@@ -582,17 +827,17 @@ def run_profile_case(which):
     ext = load_attention_extension()
     with torch.no_grad():
         if which == "prefill":
-            q, k, v = make_prefill(torch, 0)
+            q, k, v = make_prefill(torch)
             for _ in range(3):
                 ext.attention_forward(q, k, v, 0)
         elif which == "backward":
-            q, k, v = make_prefill(torch, 0)
+            q, k, v = make_prefill(torch)
             out, lse = ext.attention_forward(q, k, v, 0)
             dout = torch.randn_like(out)
             for _ in range(3):
                 ext.attention_backward(q, k, v, dout, out, lse, 0)
         else:
-            q, k, v, lens = make_decode(torch, 0)
+            q, k, v, lens = make_decode(torch)
             for _ in range(3):
                 ext.attention_forward(q, k, v, DECODE_CFG["Tk"] - 1, None, lens)
     torch.cuda.synchronize()
@@ -606,7 +851,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("prefill", "decode", "generation"), default="prefill")
-    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU work for the cpu_baseline block of our line")
+    ap.add_argument("--cpu-step-budget", type=float, default=6.0,
+                    help="reference arm: largest CPU time one step may take")
+    ap.add_argument("--no-generation", action="store_true",
+                    help="leave the config-5 generation block out of the default line")
     ap.add_argument("--profile", choices=("prefill", "decode", "backward"), default=None,
                     help="run 3 launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()

@@ -11,18 +11,24 @@
 //   warps 0-3   softmax + epilogue of tile 0 (thread = query row = TMEM lane)
 //   warps 4-7   softmax + epilogue of tile 1
 //   warp  8     TMA producer: Q tiles once, then K/V tiles through a STAGES-deep ring
-//   warp  9     S issuer for both tiles: S_t(j) = Q_t.K(j)^T as soon as K(j) has landed and
-//               the tile's softmax has read S_t(j-1), so the tensor core computes the next
-//               scores while the softmax warps work on the current ones
+//   warp  9     S issuer for both tiles: S_t(j) = Q_t.K(j)^T into the next free score buffer
 //   warps 10,11 P.V issuers, one per query tile t: O_t += P_t(j).V(j) (P from TMEM) once the
 //               softmax publishes P_t(j). A tcgen05.mma blocks its issuing thread while the
 //               tensor core's queue is full (~100 cycles per instruction under load), so the S
 //               stream must not queue behind a P.V issue: separate threads keep the next S
-//               from waiting on the previous tile's P.V (measured +2.4 % over one issuer per
-//               tile issuing both).
+//               from waiting on the previous tile's P.V.
+// Score buffers: the (KV tile j, query tile t) pairs are numbered in issue order ("slots":
+// per KV tile, tile 1 then tile 0) and slot s uses TMEM buffer s % 3. The softmax writes
+// P (bf16x2) over the first 64 columns of its own scores, so it never waits for the previous
+// P.V before publishing P, and the S of slot s + 3 is issued once the P.V of slot s has read
+// its buffer: the tensor core computes the next scores of a tile while its softmax still works
+// on the current ones, and one slow warp no longer holds back the next S of its tile.
 // Registers: launched at 168 per thread (384 threads, the 64K register file); the producer
-// warpgroup drops to 56 and the softmax warpgroups rise to 224 (2 x 224 + 56 = 504 <= 3 x 168).
-// TMEM (all 512 columns): S_t at [128t, 128t+128), P_t (bf16x2) at 256 + 64t, O_t at 384 + 64t.
+// warpgroup drops to 88 and the softmax warpgroups rise to 208 (2 x 208 + 88 = 504 <= 3 x 168;
+// with P stored in 32-score chunks the softmax needs no more, and the issuers' slot
+// bookkeeping spills below 88).
+// TMEM (all 512 columns): score / P buffers at [128b, 128b + 128) for b = 0, 1, 2, O_t at
+// 384 + 64t.
 #pragma once
 
 #include <cuda.h>
@@ -45,14 +51,16 @@ constexpr int LOAD_WARP = SOFTMAX_WARPS;
 constexpr int MMA_WARP = SOFTMAX_WARPS + 1;  // S issuer; MMA_WARP + 1 + t issues P.V of tile t
 constexpr int THREADS = (SOFTMAX_WARPS + 4) * 32;  // three full warpgroups
 constexpr uint32_t LAUNCH_REGS = 168;    // registers per thread at launch (65536 / 384, rounded)
-constexpr uint32_t SOFTMAX_REGS = 224;
-constexpr uint32_t PRODUCER_REGS = 56;
+constexpr uint32_t SOFTMAX_REGS = 208;
+constexpr uint32_t PRODUCER_REGS = 88;
 static_assert(2 * SOFTMAX_REGS + PRODUCER_REGS <= 3 * LAUNCH_REGS,
               "register hand-over exceeds the launch allocation");
 static_assert(THREADS * LAUNCH_REGS <= 65536, "launch allocation exceeds the register file");
 constexpr uint32_t TILE_BYTES = BM * HD * 2;  // 16 KiB, one 128x64 bf16 tile
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_COL = 0, P_COL = 256, O_COL = 384;
+constexpr int SBUF = 3;                  // rotating score / P buffers shared by both tiles
+constexpr uint32_t O_COL = SBUF * BN;    // O_t at O_COL + 64t
+static_assert(O_COL + TILES * HD <= TMEM_COLS, "TMEM layout exceeds 512 columns");
 constexpr float LN2 = 0.69314718055994530942f;
 // O is rescaled only when the running row max grows by more than this (log2 units);
 // between rescales P stays below 2^8, far inside the FP32/BF16 range.
@@ -65,7 +73,10 @@ struct alignas(1024) Smem {
   uint64_t q_full;
   uint64_t k_full[STAGES], k_empty[STAGES];
   uint64_t v_full[STAGES], v_empty[STAGES];
-  uint64_t s_full[TILES], s_free[TILES], p_ready[TILES], pv_done[TILES];
+  uint64_t s_full[SBUF];   // scores of the buffer's current slot are in TMEM
+  uint64_t p_ready[SBUF];  // its P is in TMEM (and O rescaled if needed): 4 warp arrivals
+  uint64_t buf_free[SBUF]; // the P.V that read the buffer's P has completed
+  uint64_t o_done[TILES];  // P.V of tile t completed (once per KV tile)
   uint64_t drain[TILES + 1];  // one per issuing thread
   uint32_t tmem_base;
   volatile int abort;
@@ -110,6 +121,14 @@ __device__ __forceinline__ int kv_tiles_for(const Params& p, int q0) {
   const long long end =
       min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + BM + p.past_len);
   return static_cast<int>((end + BN - 1) / BN);
+}
+
+// Issue-order number of the pair (KV tile j, query tile t): per KV tile, tile 1 (if it needs
+// j) then tile 0 (if it needs j). Tile 1 needs at least as many KV tiles as tile 0 unless it
+// lies past Tq (n1 == 0), so the pairs before (j, t) are min(j, n0) + min(j, n1), plus tile 1's
+// pair of the same KV tile when t == 0.
+__device__ __forceinline__ int slot_of(int j, int t, int n0, int n1) {
+  return min(j, n0) + min(j, n1) + ((t == 0 && j < n1) ? 1 : 0);
 }
 
 // Row maximum of the 128 scores: a 3-input max tree, depth ~6 instead of a 127-long chain.
@@ -159,41 +178,6 @@ __device__ __forceinline__ void exp2_poly2(float a, float b, float& pa, float& p
 // Of every 8 consecutive score pairs, this many take the FMA-pipe exp2; the rest use MUFU.
 constexpr int POLY_PAIRS_PER_8 = 3;
 
-// p = exp2(x * sl2 - m) for the 128 scores of this row: packed f32x2 FMA for the argument,
-// MUFU ex2 (or the FMA-pipe polynomial for POLY_PAIRS_PER_8 of every 8 pairs), bf16x2
-// packing into `pk`, and the FP32 row sum over 8 independent packed accumulators. Returns
-// the row sum.
-__device__ __forceinline__ float exp_pack_sum(const float (&x)[BN], float sl2, float m,
-                                              uint32_t (&pk)[BN / 2]) {
-  const uint64_t sc2 = f2_pack(sl2, sl2);
-  const uint64_t nm2 = f2_pack(-m, -m);
-  uint64_t acc[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0;
-#pragma unroll
-  for (int c = 0; c < BN / 2; ++c) {
-    float t0, t1;
-    f2_unpack(f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2), t0, t1);
-    float p0, p1;
-    if ((c & 7) < POLY_PAIRS_PER_8) {
-      exp2_poly2(t0, t1, p0, p1);
-    } else {
-      p0 = ex2_approx(t0);
-      p1 = ex2_approx(t1);
-    }
-    acc[c & 7] = f2_add(acc[c & 7], f2_pack(p0, p1));
-    pk[c] = pack_bf16x2(p0, p1);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) acc[i] = f2_add(acc[i], acc[i + 4]);
-  acc[0] = f2_add(acc[0], acc[2]);
-  acc[1] = f2_add(acc[1], acc[3]);
-  acc[0] = f2_add(acc[0], acc[1]);
-  float lo, hi;
-  f2_unpack(acc[0], lo, hi);
-  return lo + hi;
-}
-
 __device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr,
                                             uint32_t idesc) {
   // K = 64 features = 4 UMMA k-steps of 16; each step advances 32 bytes inside the
@@ -217,13 +201,56 @@ __device__ __forceinline__ void issue_pv_mma(uint32_t tmem_o, uint32_t tmem_p, u
   }
 }
 
+// p = exp2(x * sl2 - m) for the 128 scores of this row: packed f32x2 FMA for the argument,
+// MUFU ex2 (or the FMA-pipe polynomial for POLY_PAIRS_PER_8 of every 8 pairs), bf16x2 packing,
+// and the FP32 row sum over 8 independent packed accumulators. P goes to TMEM (16 columns per
+// chunk of 32 scores) as soon as each chunk is packed, over the first 64 columns of the row's
+// own score buffer (already read into x); the caller issues tcgen05.wait::st before publishing
+// P. Returns the row sum.
+__device__ __forceinline__ float exp_store_sum(const float (&x)[BN], float sl2, float m,
+                                               uint32_t t_p) {
+  const uint64_t sc2 = f2_pack(sl2, sl2);
+  const uint64_t nm2 = f2_pack(-m, -m);
+  uint64_t acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0;
+#pragma unroll
+  for (int chunk = 0; chunk < BN / 32; ++chunk) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int c = chunk * 16 + i;
+      float t0, t1;
+      f2_unpack(f2_fma(f2_pack(x[2 * c], x[2 * c + 1]), sc2, nm2), t0, t1);
+      float p0, p1;
+      if ((c & 7) < POLY_PAIRS_PER_8) {
+        exp2_poly2(t0, t1, p0, p1);
+      } else {
+        p0 = ex2_approx(t0);
+        p1 = ex2_approx(t1);
+      }
+      acc[c & 7] = f2_add(acc[c & 7], f2_pack(p0, p1));
+      pk[i] = pack_bf16x2(p0, p1);
+    }
+    tmem_st16(t_p + chunk * 16, pk);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = f2_add(acc[i], acc[i + 4]);
+  acc[0] = f2_add(acc[0], acc[2]);
+  acc[1] = f2_add(acc[1], acc[3]);
+  acc[0] = f2_add(acc[0], acc[1]);
+  float lo, hi;
+  f2_unpack(acc[0], lo, hi);
+  return lo + hi;
+}
+
 // Softmax + epilogue for query tile t (128 rows); executed by the 4 warps of that tile.
+// n0 / n1: KV tiles query tiles 0 / 1 need (they fix the slot numbering).
 __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t tmem, int t,
-                                             int wq, int lane, int bh, int q0, int n_kv) {
+                                             int wq, int lane, int bh, int q0, int n0, int n1) {
+  const int n_kv = t == 0 ? n0 : n1;
   const int r = wq * 32 + lane;  // query row within the tile == TMEM lane
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-  const uint32_t t_s = tmem + lane_base + S_COL + t * BN;
-  const uint32_t t_p = tmem + lane_base + P_COL + t * (BN / 2);
   const uint32_t t_o = tmem + lane_base + O_COL + t * HD;
   const long long row_limit = static_cast<long long>(q0) + r + p.past_len;  // last visible key
   const long long tile_limit = static_cast<long long>(q0) + p.past_len;     // row 0's limit
@@ -233,7 +260,11 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
   bool ok = true;
 
   for (int j = 0; j < n_kv; ++j) {
-    if (!warp_wait(s, &s.s_full[t], j & 1)) { ok = false; break; }
+    const int slot = slot_of(j, t, n0, n1);
+    const int buf = slot % SBUF;
+    const uint32_t use = static_cast<uint32_t>(slot / SBUF);
+    const uint32_t t_s = tmem + lane_base + buf * BN;
+    if (!warp_wait(s, &s.s_full[buf], use & 1)) { ok = false; break; }
     tc_fence_after();
     float x[BN];
     {
@@ -248,9 +279,6 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
         for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(raw[c][i]);
       }
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&s.s_free[t]);
 
     const long long kv0 = static_cast<long long>(j) * BN;
     if (kv0 + BN - 1 > tile_limit) {
@@ -270,45 +298,34 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
       m_run = m_new;
     }
     const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-    uint32_t pk[BN / 2];
-    const float rowsum = exp_pack_sum(x, sl2, m_use, pk);
+    const float rowsum = exp_store_sum(x, sl2, m_use, t_s);
     l_run = l_run * factor + rowsum;
 
-    if (j > 0) {
-      // P_t and O_t are still in use by P.V of the previous KV tile until pv_done flips.
-      if (!warp_wait(s, &s.pv_done[t], (j - 1) & 1)) { ok = false; break; }
+    if (j > 0 && __any_sync(0xffffffffu, need)) {
+      // O_t holds the P.V sums up to KV tile j - 1 once that P.V has completed; it must be
+      // rescaled to the new running max before P.V of tile j (issued after p_ready) adds to it.
+      if (!warp_wait(s, &s.o_done[t], (j - 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      if (__any_sync(0xffffffffu, need)) {
-        uint32_t o[HD / 32][32];
+      uint32_t o[HD / 32][32];
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
-        tmem_wait_ld();
+      for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
+      tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          reg_fence(o[c]);
+      for (int c = 0; c < HD / 32; ++c) {
+        reg_fence(o[c]);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * factor);
-          tmem_st32(t_o + c * 32, o[c]);
-        }
+        for (int i = 0; i < 32; ++i)
+          o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * factor);
+        tmem_st32(t_o + c * 32, o[c]);
       }
-    }
-    {
-      uint32_t half[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) half[i] = pk[i];
-      tmem_st32(t_p, half);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) half[i] = pk[32 + i];
-      tmem_st32(t_p + 32, half);
     }
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&s.p_ready[t]);
+    if (lane == 0) mbar_arrive(&s.p_ready[buf]);
   }
 
-  if (ok && n_kv > 0 && warp_wait(s, &s.pv_done[t], (n_kv - 1) & 1)) {
+  if (ok && n_kv > 0 && warp_wait(s, &s.o_done[t], (n_kv - 1) & 1)) {
     tc_fence_after();
     const int row = q0 + r;
     const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -372,11 +389,13 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], TILES);
     }
+    for (int b = 0; b < SBUF; ++b) {
+      mbar_init(&s.s_full[b], 1);
+      mbar_init(&s.p_ready[b], 4);  // the 4 softmax warps of the slot's tile
+      mbar_init(&s.buf_free[b], 1);
+    }
     for (int t = 0; t < TILES; ++t) {
-      mbar_init(&s.s_full[t], 1);
-      mbar_init(&s.s_free[t], 4);
-      mbar_init(&s.p_ready[t], 4);
-      mbar_init(&s.pv_done[t], 1);
+      mbar_init(&s.o_done[t], 1);
       mbar_init(&s.drain[t], 1);
     }
     mbar_init(&s.drain[TILES], 1);
@@ -426,10 +445,11 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
           mbar_wait(&s.v_full[j % STAGES], (j / STAGES) & 1);
       }
     } else if (warp == MMA_WARP && lane == 0) {
-      // S issuer for both query tiles. A tile that does not need KV tile j (the first one
-      // lies on the diagonal, the second past Tq) still releases the K stage once. Tile 1 is
-      // served first: on diagonal blocks it has one more KV tile, so its chain ends the CTA
-      // (cfg3: 172.0 -> 170.0 us against tile 0 first; alternating per step 179 us).
+      // S issuer for both query tiles, in slot order. A tile that does not need KV tile j (the
+      // first one lies on the diagonal, the second past Tq) still releases the K stage once.
+      // Tile 1 is served first: on diagonal blocks it has one more KV tile, so its chain ends
+      // the CTA. The S of a slot goes into buffer slot % 3 once the P.V that read that
+      // buffer's previous P (slot - 3) has completed.
       const uint32_t idesc_s = make_idesc_bf16(BM, BN, false);
       bool ok = wait_or_abort(s, &s.q_full, 0);
       for (int j = 0; ok && j < n_load; ++j) {
@@ -438,10 +458,16 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int tt = 0; tt < TILES; ++tt) {
           const int t = TILES - 1 - tt;
           if (j < n_kv[t]) {
-            if (j > 0 && !wait_or_abort(s, &s.s_free[t], (j - 1) & 1)) { ok = false; break; }
+            const int slot = slot_of(j, t, n_kv[0], n_kv[1]);
+            const int buf = slot % SBUF;
+            const uint32_t use = static_cast<uint32_t>(slot / SBUF);
+            if (use > 0 && !wait_or_abort(s, &s.buf_free[buf], (use - 1) & 1)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
-            issue_s_mma(tmem + S_COL + t * BN, smem_u32(s.q[t]), smem_u32(s.k[st]), idesc_s);
-            umma_commit(&s.s_full[t]);
+            issue_s_mma(tmem + buf * BN, smem_u32(s.q[t]), smem_u32(s.k[st]), idesc_s);
+            umma_commit(&s.s_full[buf]);
             umma_commit(&s.k_empty[st]);
           } else {
             mbar_arrive(&s.k_empty[st]);
@@ -458,15 +484,18 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
       const int t = warp - MMA_WARP - 1;
       const int n = n_kv[t];
       const uint32_t idesc_o = make_idesc_bf16(BM, HD, true);
-      const uint32_t t_p = tmem + P_COL + t * (BN / 2);
       const uint32_t t_o = tmem + O_COL + t * HD;
       for (int j = 0; j < n; ++j) {
         const int st = j % STAGES;
+        const int slot = slot_of(j, t, n_kv[0], n_kv[1]);
+        const int buf = slot % SBUF;
+        const uint32_t use = static_cast<uint32_t>(slot / SBUF);
         if (!wait_or_abort(s, &s.v_full[st], (j / STAGES) & 1)) break;
-        if (!wait_or_abort(s, &s.p_ready[t], j & 1)) break;
+        if (!wait_or_abort(s, &s.p_ready[buf], use & 1)) break;
         tc_fence_after();
-        issue_pv_mma(t_o, t_p, smem_u32(s.v[st]), idesc_o, j > 0);
-        umma_commit(&s.pv_done[t]);
+        issue_pv_mma(t_o, tmem + buf * BN, smem_u32(s.v[st]), idesc_o, j > 0);
+        umma_commit(&s.buf_free[buf]);
+        umma_commit(&s.o_done[t]);
         umma_commit(&s.v_empty[st]);
       }
       for (int j = n; j < n_load && !s.abort; ++j) {
@@ -480,7 +509,7 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
   } else {
     regs_increase<SOFTMAX_REGS>();
     const int t = warp / 4;
-    softmax_tile(s, p, tmem, t, warp % 4, lane, bh, q0[t], n_kv[t]);
+    softmax_tile(s, p, tmem, t, warp % 4, lane, bh, q0[t], n_kv[0], n_kv[1]);
   }
 
   tc_fence_before();

@@ -465,7 +465,12 @@ def request(model: Decoder, prompt: torch.Tensor, new_tokens: int, graphed: bool
     """One timed request (benchmarks/model.py:19-37): cache allocation, prefill through the first
     token (TTFT), then the remaining decode steps with no per-token host synchronisation
     (TPOT). Host wall time around device synchronisations. In graphed mode the capture of the
-    decode step happens before the timer starts, as a serving loop would hold the graph."""
+    decode step happens before the timer starts, as a serving loop would hold the graph.
+
+    Entering ``torch.cuda.graph`` empties the caching allocator (``torch.cuda.empty_cache``),
+    so the first eager prefill after a capture would allocate every activation buffer through
+    cudaMalloc again. One untimed prefill after the capture brings the allocator back to the
+    state a serving loop runs in; without it the graphed TTFT measured the re-allocation."""
     device = prompt.device
     g = None
     if graphed:
@@ -475,6 +480,8 @@ def request(model: Decoder, prompt: torch.Tensor, new_tokens: int, graphed: bool
         g = GraphedDecode(model, cache, new_tokens)
         g.prepare(token)
         g.capture()
+        cache.reset()
+        model(prompt, cache=cache, last_only=True)
         cache.reset()
     _sync(device)
     start = time.perf_counter()
