@@ -67,16 +67,31 @@ def load_peaks():
             "source": "fallback"}
 
 
+# Source file of each kernel whose DRAM traffic profiles/traffic.txt records.
+KERNEL_SOURCES = {"attention_prefill_kernel": "prefill_sm100.cuh",
+                  "decode_split_kernel": "decode_sm100.cuh"}
+
+
+def kernel_source_hash(kernel):
+    """First 16 hex digits of the SHA-256 of the kernel's source file."""
+    import hashlib
+    path = os.path.join(ROOT, "tiny-transformer_b200", "csrc", KERNEL_SOURCES[kernel])
+    return hashlib.sha256(open(path, "rb").read()).hexdigest()[:16]
+
+
 def load_traffic():
     """Per-launch DRAM bytes of the dominant kernels from the committed ncu summaries
-    (profiles/traffic.txt: `<kernel> <bytes per launch>` lines), or {} when absent."""
+    (profiles/traffic.txt: `<kernel> <bytes per launch> <source hash>` lines). A figure whose
+    source hash no longer matches the kernel's source was measured on other code: it is
+    reported as None (stale) rather than carried over."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")
     out = {}
     if os.path.exists(path):
         for line in open(path):
             parts = line.split("#")[0].split()
-            if len(parts) == 2:
-                out[parts[0]] = float(parts[1])
+            if len(parts) == 3 and parts[0] in KERNEL_SOURCES:
+                fresh = parts[2] == kernel_source_hash(parts[0])
+                out[parts[0]] = float(parts[1]) if fresh else None
     return out
 
 

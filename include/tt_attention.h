@@ -76,11 +76,12 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     void* workspace, size_t workspace_bytes,
     void* stream);
 
-/* Scratch bytes tt_attn_forward_bf16 needs for this shape: for decode, a 256-byte work
- * counter, plus (when sequences are split into more than one chunk) one 4-byte arrival counter
- * per (batch, head) rounded up to 256 bytes and 272 bytes of FP32 partial per (batch, head,
- * chunk). Replaces the partials tensor the reference allocates (attention.cu:128-129).
- * Returns 0 for prefill shapes and for invalid shapes. */
+/* Scratch bytes tt_attn_forward_bf16 needs for this shape: for decode of a cache longer than
+ * 1024 keys, a 256-byte work counter, plus (when sequences are split into more than one chunk)
+ * one 4-byte arrival counter per (batch, head) rounded up to 256 bytes and 272 bytes of FP32
+ * partial per (batch, head, chunk). Replaces the partials tensor the reference allocates
+ * (attention.cu:128-129). Returns 0 for decode of caches of up to 1024 keys (one CTA per
+ * sequence, no scratch), for prefill shapes and for invalid shapes. */
 TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, int64_t q_len,
                                                   int64_t kv_len);
 
@@ -198,10 +199,13 @@ TT_ATTN_API int tt_attn_abi_version(void);
  * Same computation and arguments as tt_attn_forward_bf16 with q_len = 1, head_dim = 64 and
  * past_len = kv_len - 1; the split-KV partials live in a static device array of 8 MiB
  * (8388608 bytes) that every GPU loading this library holds until exit. Shapes whose partials
- * exceed it (tt_attn_forward_workspace_size) return TT_ATTN_BAD_ARG. The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture. All calls share the array:
- * calls whose kernels overlap on the GPU (different streams, or different host threads) race
- * on it and must be serialised by the caller.
+ * exceed it (tt_attn_forward_workspace_size) return TT_ATTN_BAD_ARG; a device other than
+ * sm_100 returns TT_ATTN_UNSUPPORTED. The first call on a device looks up the array's device
+ * address (with that device current), and so does the first call after the current context
+ * of that device changed (cudaDeviceReset, or a context the caller made current); make those
+ * calls before any stream capture. All calls share the array: calls whose kernels overlap on
+ * the GPU (different streams, or different host threads) race on it and must be serialised
+ * by the caller. Caches of up to 1024 keys use no scratch at all.
  */
 TT_ATTN_API tt_attn_status tt_attn_decode_bf16_noalloc(
     const void* q, const int64_t* q_strides,

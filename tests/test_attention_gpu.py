@@ -266,12 +266,13 @@ def test_unaligned_and_strided_views(ext):
 
 
 def test_decode_split_boundaries_and_rescaling(ext):
-    # reference :289-310, boundaries of 32-row warp slices, 384-key ring stages (the two-stage
-    # ring wraps at 768) and 384-key work items (six heads always take the smallest item),
-    # and long caches.
+    # reference :289-310. Caches of up to 4096 keys take the cluster kernel: boundaries of its
+    # 32-row warp slices, 128-key passes and 1..8 CTAs per sequence (two passes per CTA past
+    # 1024 keys, four past 3072). Longer ones take the persistent split-KV kernel: 384-key ring
+    # stages, 384-key work items (six heads always take the smallest item) and long caches.
     for tk in (1, 2, 7, 31, 32, 33, 63, 64, 65, 127, 128, 129, 255, 256, 257, 383, 384, 385,
-               511, 512, 513, 767, 768, 769, 1151, 1152, 1153, 1535, 1536, 1537, 3072, 3073,
-               4095, 4096, 4097, 8192, 8193):
+               511, 512, 513, 767, 768, 769, 1023, 1024, 1025, 1151, 1152, 1153, 1535, 1536,
+               1537, 3072, 3073, 4095, 4096, 4097, 8192, 8193):
         q = torch.randn(2, 3, 1, 64, device="cuda", dtype=torch.bfloat16)
         k, v = [torch.randn(2, 3, tk, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
         check_forward(ext, q, k, v, tk - 1)
@@ -434,15 +435,16 @@ def test_rejects_sequence_index_overflow_before_copy(ext):
             ext.attention_forward(q, kv, kv, tk - tq)
 
 
-@pytest.mark.parametrize("tk,chunk", [(769, 768), (1536, 768), (1537, 1536), (3073, 1536),
-                                      (4608, 1536)])
-def test_decode_work_item_sizes(ext, tk, chunk):
-    """Enough heads (50 x 12) that the host picks 768- and 1536-key work items: sequence ends on
-    and beside item boundaries, with and without kv_lens. The chosen item size is read back
-    from the workspace the C ABI asks for (a work counter, one arrival counter per (batch, head)
-    rounded up to 256 bytes, and one 272-byte partial per item)."""
+@pytest.mark.parametrize("B,tk,chunk", [(90, 1025, 768), (90, 1536, 768), (100, 1537, 1536),
+                                        (50, 3073, 1536), (50, 4608, 1536), (30, 4097, 768)])
+def test_decode_work_item_sizes(ext, B, tk, chunk):
+    """Caches large enough (over 2^20 (batch * head * key) rows, or over 4096 keys) for the
+    persistent split-KV kernel, and enough heads that the host picks 768- and 1536-key work
+    items: sequence ends on and beside item boundaries, with and without kv_lens. The chosen
+    item size is read back from the workspace the C ABI asks for (a work counter, one arrival
+    counter per (batch, head) rounded up to 256 bytes, and one 272-byte partial per item)."""
     from tiny_transformer_b200.operators._extension import load_c_abi
-    B, H = 50, 12
+    H = 12
     n_items = -(-tk // chunk)
     arrivals = -(-B * H * 4 // 256) * 256
     assert (load_c_abi().tt_attn_forward_workspace_size(B, H, 1, tk)

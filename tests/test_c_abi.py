@@ -83,15 +83,24 @@ def test_unsupported_layouts(lib):
 
 
 def test_workspace_and_layout_queries(lib):
-    # Decode with enough keys splits into several chunks and needs partials.
-    n = lib.tt_attn_forward_workspace_size(8, 12, 1, 4096)
-    arrivals = -(-8 * 12 * 4 // 256) * 256        # one counter per (batch, head), 256-B rounded
+    # Decode of a large cache (the persistent split-KV kernel) splits into several chunks and
+    # needs partials.
+    n = lib.tt_attn_forward_workspace_size(64, 12, 1, 4096)
+    arrivals = -(-64 * 12 * 4 // 256) * 256       # one counter per (batch, head), 256-B rounded
     assert n > 256 + arrivals and (n - 256 - arrivals) % (68 * 4) == 0  # counters + partials
-    assert lib.tt_attn_forward_workspace_size(8, 12, 1, 16) == 256  # one chunk: counter only
+    # Caches of up to 4096 keys with at most 2^20 (batch * head * key) rows take the cluster
+    # kernel: no workspace.
+    assert lib.tt_attn_forward_workspace_size(8, 12, 1, 16) == 0
+    assert lib.tt_attn_forward_workspace_size(8, 12, 1, 4096) == 0
+    assert lib.tt_attn_forward_workspace_size(256, 1, 1, 4096) == 0
+    assert lib.tt_attn_forward_workspace_size(257, 1, 1, 4096) > 0
+    assert lib.tt_attn_forward_workspace_size(1, 1, 1, 4097) > 0
+    # Enough sequences that each takes one 1536-key item: the work counter only.
+    assert lib.tt_attn_forward_workspace_size(100, 12, 1, 1500) == 256
     assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # prefill needs none
     assert lib.tt_attn_forward_workspace_size(0, 12, 1, 512) == 0
     # Missing workspace for a split decode is rejected.
-    assert _call(lib, B=8, H=12, tq=1, tk=4096, past=4095) == 1
+    assert _call(lib, B=64, H=12, tq=1, tk=4096, past=4095) == 1
     assert "workspace" in _err(lib)
     assert lib.tt_attn_layout_supported(16, _strides(4096, 4096, 64, 1)) == 1
     assert lib.tt_attn_layout_supported(17, _strides(4096, 4096, 64, 1)) == 0
@@ -136,3 +145,19 @@ def test_backward_unsupported_layout_and_workspace_size(lib):
     # -LSE * log2(e) and -D for 6 heads x 128 padded rows, then the 30 x 64 FP32 dQ accumulator.
     assert lib.tt_attn_backward_workspace_size(2, 3, 5) == 2 * 6 * 128 * 4 + 2 * 3 * 5 * 64 * 4
     assert lib.tt_attn_backward_workspace_size(0, 3, 5) == 0
+
+
+def test_no_alloc_argument_checks_before_any_cuda_call(lib):
+    """The no-allocation decode rejects non-positive sizes and shapes whose partials exceed its
+    8 MiB scratch before touching CUDA (no GPU in this process)."""
+    fn = lib.tt_attn_decode_bf16_noalloc
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, i64p, ctypes.c_void_p, i64p, ctypes.c_void_p, i64p,
+                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    st = _strides(64, 64, 64, 1)
+    assert fn(16, st, 16, st, 16, st, 0, 12, 100, None, 16, 16, None) == 1
+    assert "positive" in _err(lib)
+    assert fn(16, st, 16, st, 16, st, 64, 12, 1 << 20, None, 16, 16, None) == 1
+    assert "at most 8388608 bytes" in _err(lib)

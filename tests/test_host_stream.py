@@ -18,6 +18,19 @@ def test_rejects_unpinned_and_device_inputs():
         attention_from_host(x, x, x)
 
 
+def test_rejects_bad_arguments_before_any_copy():
+    # Checked before the pinned-memory check, i.e. before anything is allocated or queued.
+    q = torch.zeros(1, 2, 8, 64, dtype=torch.bfloat16)
+    k = torch.zeros(1, 2, 10, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="Tk == past_len"):
+        attention_from_host(q, k, k, 0)
+    with pytest.raises(RuntimeError, match="non-negative"):
+        attention_from_host(q, q, q, -1)
+    w = torch.zeros(1, 2, 8, 32, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="head_dim=64"):
+        attention_from_host(w, w, w, 0)
+
+
 gpu = pytest.mark.gpu
 
 

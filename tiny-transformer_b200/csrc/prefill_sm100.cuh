@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "sm100_ptx.cuh"
 
@@ -259,12 +260,14 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
   float l_run = 0.f;        // running sum of exp2(x - m_run)
   bool ok = true;
 
-  for (int j = 0; j < n_kv; ++j) {
+  // One KV step j of this tile; `masked` (std::true_type / std::false_type) selects the causal
+  // mask at compile time. Returns false when a wait gave up (the CTA is aborting).
+  auto step = [&](auto masked, int j) -> bool {
     const int slot = slot_of(j, t, n0, n1);
     const int buf = slot % SBUF;
     const uint32_t use = static_cast<uint32_t>(slot / SBUF);
     const uint32_t t_s = tmem + lane_base + buf * BN;
-    if (!warp_wait(s, &s.s_full[buf], use & 1)) { ok = false; break; }
+    if (!warp_wait(s, &s.s_full[buf], use & 1)) return false;
     tc_fence_after();
     float x[BN];
     {
@@ -281,7 +284,7 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
     }
 
     const long long kv0 = static_cast<long long>(j) * BN;
-    if (kv0 + BN - 1 > tile_limit) {
+    if constexpr (decltype(masked)::value) {
 #pragma unroll
       for (int c = 0; c < BN; ++c)
         if (kv0 + c > row_limit) x[c] = -INFINITY;
@@ -304,7 +307,7 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
     if (j > 0 && __any_sync(0xffffffffu, need)) {
       // O_t holds the P.V sums up to KV tile j - 1 once that P.V has completed; it must be
       // rescaled to the new running max before P.V of tile j (issued after p_ready) adds to it.
-      if (!warp_wait(s, &s.o_done[t], (j - 1) & 1)) { ok = false; break; }
+      if (!warp_wait(s, &s.o_done[t], (j - 1) & 1)) return false;
       tc_fence_after();
       uint32_t o[HD / 32][32];
 #pragma unroll
@@ -323,7 +326,18 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.p_ready[buf]);
-  }
+    return true;
+  };
+  // Interior KV tiles (every key visible to every row of the tile) and the diagonal tiles
+  // are separate compile-time instantiations of the step: only the latter carry the mask.
+  const int n_full = static_cast<int>(
+      min(static_cast<long long>(n_kv), max(0LL, tile_limit + 1) / BN));
+  int jj = 0;
+  for (; jj < n_full; ++jj)
+    if (!step(std::false_type{}, jj)) { ok = false; break; }
+  if (ok)
+    for (; jj < n_kv; ++jj)
+      if (!step(std::true_type{}, jj)) { ok = false; break; }
 
   if (ok && n_kv > 0 && warp_wait(s, &s.o_done[t], (n_kv - 1) & 1)) {
     tc_fence_after();

@@ -18,6 +18,7 @@
 #include "sm100_ptx.cuh"
 #include "prefill_sm100.cuh"
 #include "decode_sm100.cuh"
+#include "decode_direct_sm100.cuh"
 #include "selftest_sm100.cuh"
 #include "rope_append_sm100.cuh"
 #include "backward_sm100.cuh"
@@ -70,6 +71,17 @@ int decode_chunk(int64_t bh, int64_t tk) {
   while (chunk > tt::decode::MIN_CHUNK && bh * ((tk + chunk - 1) / chunk) < kTargetItems)
     chunk /= 2;
   return chunk;
+}
+
+// Decode path choice (shape only, so the workspace size never depends on the device): the
+// cluster kernel (decode_direct_sm100.cuh: no workspace, one launch, <= 8 CTAs per sequence)
+// unless the cache is long and the whole K/V read large, where the persistent split-KV kernel
+// (decode_sm100.cuh) streams closer to the HBM bandwidth.
+constexpr int64_t kDirectDecodeMaxKeys = 4096;
+constexpr int64_t kDirectDecodeMaxRows = int64_t(1) << 20;  // (batch * heads * kv_len): 256 MB of K/V
+
+bool use_direct_decode(int64_t bh, int64_t kv_len) {
+  return kv_len <= kDirectDecodeMaxKeys && bh * kv_len <= kDirectDecodeMaxRows;
 }
 
 // Bytes of the per-sequence arrival counters of a split decode (one unsigned per (batch, head),
@@ -283,6 +295,8 @@ TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, 
                                                   int64_t kv_len) {
   if (batch <= 0 || heads <= 0 || q_len != 1 || kv_len <= 0 || kv_len > INT32_MAX) return 0;
   if (batch > INT32_MAX / heads) return 0;
+  // Short and medium caches take the cluster kernel, which needs no workspace.
+  if (use_direct_decode(batch * heads, kv_len)) return 0;
   const int64_t bh = batch * heads;
   const int chunk = decode_chunk(bh, kv_len);
   const int64_t n_chunks = (kv_len + chunk - 1) / chunk;
@@ -661,6 +675,50 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
   if (st != TT_ATTN_OK) return st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
 
+  if (is_decode && use_direct_decode(bh, kv_len)) {
+    // One cluster of `splits` CTAs per (batch, head); no workspace, one launch.
+    namespace dd = tt::decode_direct;
+    tt::decode_direct::Params p{};
+    p.q = static_cast<const __nv_bfloat16*>(q);
+    p.k = static_cast<const __nv_bfloat16*>(k);
+    p.v = static_cast<const __nv_bfloat16*>(v);
+    p.q_sb = qs.stride[0];
+    p.q_sh = qs.stride[1];
+    p.k_sb = ks.stride[0];
+    p.k_sh = ks.stride[1];
+    p.k_st = ks.stride[2];
+    p.v_sb = vs.stride[0];
+    p.v_sh = vs.stride[1];
+    p.v_st = vs.stride[2];
+    p.kv_lens = kv_lens;
+    p.B = static_cast<int>(batch);
+    p.H = static_cast<int>(heads);
+    p.Tk = static_cast<int>(kv_len);
+    const int64_t passes_total = (kv_len + dd::KEYS_PER_PASS - 1) / dd::KEYS_PER_PASS;
+    p.splits = static_cast<int>(std::min<int64_t>(dd::MAX_SPLITS, passes_total));
+    p.keys_per_cta =
+        static_cast<int>((passes_total + p.splits - 1) / p.splits) * dd::KEYS_PER_PASS;
+    p.o = static_cast<__nv_bfloat16*>(out);
+    p.lse = lse;
+    p.scale_log2 = kScaleLog2;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(bh * p.splits), 1, 1);
+    cfg.blockDim = dim3(dd::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = cs;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, dd::decode_direct_kernel, p);
+    if (le != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL,
+                  std::string("decode_direct_kernel launch: ") + cudaGetErrorString(le));
+    return check_launch("decode_direct_kernel launch");
+  }
   if (is_decode) {
     tt::decode::Params p{};
     p.q = static_cast<const __nv_bfloat16*>(q);
@@ -738,9 +796,31 @@ constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB of decode par
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Host code must not use the array's name as a device address: it is a host-side stand-in.
-// The device address is fetched once per device with that device current.
-void* g_noalloc_scratch_ptr[kMaxDevices] = {};
+// The device address is fetched with the device current, and fetched again whenever the
+// thread's current context on that device is a different one (after cudaDeviceReset, or when
+// the caller made a context of its own current), since the array lives once per context.
+struct NoAllocScratch {
+  void* ctx = nullptr;  // CUcontext the address belongs to
+  void* ptr = nullptr;
+};
+NoAllocScratch g_noalloc_scratch_ptr[kMaxDevices];
 std::mutex g_noalloc_mu;
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
 }  // namespace
 
 extern "C" {
@@ -760,24 +840,30 @@ TT_ATTN_API tt_attn_status tt_attn_decode_bf16_noalloc(
                   need, kNoAllocScratchBytes);
     return fail(TT_ATTN_BAD_ARG, buf);
   }
+  // The device check first: on a device without an sm_100 image the symbol lookup below would
+  // fail with a less useful message than the forward entry point's UNSUPPORTED.
   int dev = 0;
-  const cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess)
-    return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return fail(TT_ATTN_UNSUPPORTED, "device index out of range");
+  tt_attn_status st = prepare_device(&dev);
+  if (st != TT_ATTN_OK) return st;
+  CUcontext ctx = nullptr;
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return fail(TT_ATTN_LAUNCH_FAIL, "no current CUDA context for the no-allocation scratch");
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    NoAllocScratch& slot = g_noalloc_scratch_ptr[dev];
+    if (slot.ptr == nullptr || slot.ctx != static_cast<void*>(ctx)) {
       void* ptr = nullptr;
       const cudaError_t se = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
       if (se != cudaSuccess || ptr == nullptr)
         return fail(TT_ATTN_LAUNCH_FAIL,
                     std::string("cudaGetSymbolAddress(no-allocation scratch): ") +
                         cudaGetErrorString(se));
-      g_noalloc_scratch_ptr[dev] = ptr;
+      slot.ptr = ptr;
+      slot.ctx = static_cast<void*>(ctx);
     }
-    scratch = g_noalloc_scratch_ptr[dev];
+    scratch = slot.ptr;
   }
   // Each call clears the counters it uses and writes every partial before it is read, so the
   // scratch needs no clearing between calls.

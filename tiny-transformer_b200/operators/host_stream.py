@@ -25,7 +25,8 @@ _streams_lock = threading.Lock()
 
 
 def _side_streams(device):
-    """Two non-default streams per device (input copies, output copies), created once."""
+    """Two non-default streams per device (input copies, output copies), created once.
+    ``device`` carries an explicit index (the caller normalises "cuda" to the current one)."""
     key = device.index
     with _streams_lock:
         if key not in _streams:
@@ -60,14 +61,22 @@ def attention_from_host(q, k, v, past_len=0, out=None, lse=None, slices=8, devic
     reached this point (``torch.cuda.current_stream().synchronize()``). Device memory: one
     device copy of q, k and v, plus O and LSE of one slice at a time per slice in flight.
     """
-    for name, x in (("q", q), ("k", k), ("v", v)):
-        _check_host(name, x)
+    # Shapes and the operator's own checks first: nothing is allocated or queued for a call
+    # that the operator would reject.
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise RuntimeError("attention_from_host: q, k, v must be 4-D (B, H, T, 64)")
     B, H, Tq, D = q.shape
     if tuple(k.shape[:2]) != (B, H) or k.shape != v.shape or k.shape[3] != D:
         raise RuntimeError("attention_from_host: k and v must be (B, H, Tk, D) with q's B, H, D")
     Tk = k.shape[2]
+    if D != 64:
+        raise RuntimeError("attention_from_host: attention currently supports only head_dim=64")
+    if int(past_len) < 0:
+        raise RuntimeError("attention_from_host: past_len must be non-negative")
+    if Tk < Tq or int(past_len) != Tk - Tq:
+        raise RuntimeError("attention_from_host: expected Tk == past_len + Tq")
+    for name, x in (("q", q), ("k", k), ("v", v)):
+        _check_host(name, x)
     if out is None:
         out = torch.empty((B, H, Tq, D), dtype=torch.bfloat16, pin_memory=True)
     else:
@@ -78,8 +87,12 @@ def attention_from_host(q, k, v, past_len=0, out=None, lse=None, slices=8, devic
         _check_host("lse", lse, (B, H, Tq), torch.float32)
     if int(slices) < 1:
         raise RuntimeError("attention_from_host: slices must be at least 1")
-    device = torch.device("cuda", torch.cuda.current_device()) if device is None \
-        else torch.device(device)
+    device = torch.device("cuda" if device is None else device)
+    if device.type != "cuda":
+        raise RuntimeError("attention_from_host: device must be a CUDA device")
+    if device.index is None:
+        # "cuda" without an index means the current device; the side streams are per index.
+        device = torch.device("cuda", torch.cuda.current_device())
 
     rows = B * H
     n_slices = min(int(slices), rows)

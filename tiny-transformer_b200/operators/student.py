@@ -4,7 +4,7 @@ Same signature, guards and error behaviour as Tiny-transformer's
 ``tiny_transformer/operators/student.py:190-232`` (the ``_Attention`` autograd bridge and the
 ``attention`` operator), plus one optional, additive argument ``kv_lens``. Selected in the
 reference with ``--op attention=student`` once its ``load_attention_extension`` returns this
-package's native module.
+package's native module (``tt_attention_C``, loaded by ``_extension.load_attention_extension``).
 
 Differences from the reference operator, all deliberate:
 * FP32 inputs raise (the reference ran an FP32 SIMT kernel; this path is BF16 only);
