@@ -9,9 +9,10 @@ operator, and the outputs are checked against the CPU oracle:
   116-117): O atol 2e-2 / rtol 3e-2, LSE atol 2e-4 / rtol 2e-5.
 
 Configurations: cfg1 (B=8 H=12 T=512) whole; cfg3 (B=4 H=12 T=4096) on the first, a middle and
-the last (batch, head) row of the whole-workload call and of the 8-way shards bench.py gives
-each rank; cfg4 (B=64 H=12 Tk=8192, kv_lens U[1024, 8192] by the bench seed) on every sequence;
-cfg2 (B=8 H=12 Tk=512 decode) whole.
+the last (batch, head) row of the whole-workload call, and on the 8-way shards bench.py gives
+each rank (whose long query blocks run split over their KV range); cfg4 (B=64 H=12 Tk=8192,
+kv_lens U[1024, 8192] by the bench seed) on every sequence; cfg2 (B=8 H=12 Tk=512 decode)
+whole.
 """
 import numpy as np
 import pytest
@@ -72,12 +73,17 @@ def test_cfg3_rows_whole_and_sharded(ext):
     n = flat[0].shape[0]
     for r in (0, n // 2, n - 1):
         _check(*(_np(x[r:r + 1]) for x in flat), 0)
-    # The 8-way shards the multi-GPU bench computes are bitwise the rows of the whole call.
+    # The 8-way shards the multi-GPU bench computes (6 rows each: few CTAs, so the long query
+    # blocks are split over their KV range and merged): the oracle on each shard's last row,
+    # and the whole call's rows to within the FP32 merge order.
     for shard in even_shards(n, 8):
         qs, ks, vs = (prefill_slice(x, shard) for x in (q, k, v))
         o_s, l_s = ext.attention_forward(qs, ks, vs, 0)
-        assert torch.equal(o_s, flat[0][shard.start:shard.stop])
-        assert torch.equal(l_s, flat[1][shard.start:shard.stop])
+        torch.testing.assert_close(o_s, flat[0][shard.start:shard.stop], atol=1e-2, rtol=1e-2)
+        torch.testing.assert_close(l_s, flat[1][shard.start:shard.stop], atol=1e-5, rtol=1e-6)
+        r = shard.size - 1
+        _check(_np(o_s[r:r + 1]), _np(l_s[r:r + 1]), _np(qs[r:r + 1]), _np(ks[r:r + 1]),
+               _np(vs[r:r + 1]), 0)
 
 
 @torch.no_grad()

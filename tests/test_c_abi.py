@@ -97,7 +97,18 @@ def test_workspace_and_layout_queries(lib):
     assert lib.tt_attn_forward_workspace_size(1, 1, 1, 4097) > 0
     # Enough sequences that each takes one 1536-key item: the work counter only.
     assert lib.tt_attn_forward_workspace_size(100, 12, 1, 1500) == 256
-    assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # prefill needs none
+    assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # enough CTAs: no split
+    assert lib.tt_attn_forward_workspace_size(4, 12, 4096, 4096) == 0
+    # Fewer query blocks than SMs (an 8-way shard of B=4 H=12 T=4096: 6 rows, 96 blocks): the
+    # long blocks are split into parts of at most 16 KV tiles, the smallest size whose CTAs
+    # (8 + 8 x 2 per row = 144) fit one wave of 148; the longest block (32 tiles) has 2 parts,
+    # and each row, block and part has a 272-byte record.
+    assert lib.tt_attn_forward_workspace_size(1, 6, 4096, 4096) == 6 * 16 * 2 * 256 * 272
+    # One sequence: parts of 4 tiles (72 CTAs), the longest block in 8.
+    assert lib.tt_attn_forward_workspace_size(1, 1, 4096, 4096) == 16 * 8 * 256 * 272
+    # 12 rows (192 blocks) already exceed one wave: no split.
+    assert lib.tt_attn_forward_workspace_size(1, 12, 4096, 4096) == 0
+    assert lib.tt_attn_forward_workspace_size(1, 1, 513, 512) == 0  # q_len > kv_len: invalid
     assert lib.tt_attn_forward_workspace_size(0, 12, 1, 512) == 0
     # Missing workspace for a split decode is rejected.
     assert _call(lib, B=64, H=12, tq=1, tk=4096, past=4095) == 1

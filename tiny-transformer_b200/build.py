@@ -77,6 +77,7 @@ def _prefill_launch_regs() -> int:
 
 def _check_ptxas(report: str) -> None:
     lines = report.splitlines()
+    found = 0
     for i, line in enumerate(lines):
         if "Compiling entry function" in line and "attention_prefill_kernel" in line:
             for follow in lines[i + 1:i + 4]:
@@ -88,8 +89,10 @@ def _check_ptxas(report: str) -> None:
                         raise RuntimeError(
                             f"attention_prefill_kernel compiled with {regs} registers, expected "
                             f"{want}: the setmaxnreg hand-over would not be sound")
-                    return
-    raise RuntimeError("ptxas report for attention_prefill_kernel not found")
+                    found += 1
+                    break
+    if found == 0:
+        raise RuntimeError("ptxas report for attention_prefill_kernel not found")
 
 
 def build_library(verbose: bool = False, force: bool = False) -> str:

@@ -85,12 +85,25 @@ struct alignas(1024) Smem {
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack for 1 KiB alignment
 
+// Record of one query row's partial result over one part of its KV range (split query
+// blocks only): unnormalised O[64], running max m (log2 units), row sum l, 2 pad (16-byte
+// aligned records).
+constexpr int PART_REC = HD + 4;
+
 struct Params {
   int B, H, Tq, Tk, past_len;
   int n_qblocks;     // ceil(Tq / BLOCK_M)
   __nv_bfloat16* o;  // contiguous [B, H, Tq, 64]
   float* lse;        // contiguous [B, H, Tq]
   float scale_log2;  // softmax scale * log2(e)
+  // KV split of query blocks (few CTAs for the SMs): a block of n KV tiles runs as
+  // parts = ceil(n / part_tiles) CTAs over consecutive, near-equal KV ranges
+  // [i * n / parts, (i + 1) * n / parts), each writing partial records that
+  // prefill_combine_kernel merges. part_tiles = 0: no split.
+  int part_tiles;
+  int max_parts;          // parts of the longest block (record stride), at most 32
+  int first_split_qb;     // lowest query block that is split
+  float* partials;        // [B*H, n_qblocks, max_parts, BLOCK_M, PART_REC]
 };
 
 // Bounded wait that also gives up as soon as another role has aborted.
@@ -122,6 +135,23 @@ __device__ __forceinline__ int kv_tiles_for(const Params& p, int q0) {
   const long long end =
       min(static_cast<long long>(p.Tk), static_cast<long long>(q0) + BM + p.past_len);
   return static_cast<int>((end + BN - 1) / BN);
+}
+
+// KV tiles query block qb loads (its second tile needs at least as many as its first unless
+// it lies past Tq).
+__device__ __forceinline__ int block_tiles(const Params& p, int qb) {
+  return max(kv_tiles_for(p, qb * BLOCK_M), kv_tiles_for(p, qb * BLOCK_M + BM));
+}
+
+__device__ __forceinline__ int block_parts(const Params& p, int qb) {
+  return p.part_tiles == 0 ? 1 : max(1, (block_tiles(p, qb) + p.part_tiles - 1) / p.part_tiles);
+}
+
+__device__ __forceinline__ float* part_record(const Params& p, int bh, int qb, int part,
+                                              int row_in_block) {
+  return p.partials +
+         ((static_cast<size_t>(bh) * p.n_qblocks + qb) * p.max_parts + part) * BLOCK_M * PART_REC +
+         static_cast<size_t>(row_in_block) * PART_REC;
 }
 
 // Issue-order number of the pair (KV tile j, query tile t): per KV tile, tile 1 (if it needs
@@ -246,9 +276,13 @@ __device__ __forceinline__ float exp_store_sum(const float (&x)[BN], float sl2, 
 }
 
 // Softmax + epilogue for query tile t (128 rows); executed by the 4 warps of that tile.
-// n0 / n1: KV tiles query tiles 0 / 1 need (they fix the slot numbering).
+// The CTA covers KV tiles [k0, k0 + its steps); n0 / n1: the steps query tiles 0 / 1 take in
+// it (they fix the slot numbering). A CTA of a split block (parts > 1) writes its rows'
+// partial records instead of O and LSE.
+template <bool SPLIT>
 __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t tmem, int t,
-                                             int wq, int lane, int bh, int q0, int n0, int n1) {
+                                             int wq, int lane, int bh, int qb, int q0, int n0,
+                                             int n1, int k0, int part, int parts) {
   const int n_kv = t == 0 ? n0 : n1;
   const int r = wq * 32 + lane;  // query row within the tile == TMEM lane
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
@@ -263,6 +297,7 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
   // One KV step j of this tile; `masked` (std::true_type / std::false_type) selects the causal
   // mask at compile time. Returns false when a wait gave up (the CTA is aborting).
   auto step = [&](auto masked, int j) -> bool {
+    // j: step within this CTA's KV range; k0 + j: the KV tile.
     const int slot = slot_of(j, t, n0, n1);
     const int buf = slot % SBUF;
     const uint32_t use = static_cast<uint32_t>(slot / SBUF);
@@ -283,7 +318,7 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
       }
     }
 
-    const long long kv0 = static_cast<long long>(j) * BN;
+    const long long kv0 = static_cast<long long>(k0 + j) * BN;
     if constexpr (decltype(masked)::value) {
 #pragma unroll
       for (int c = 0; c < BN; ++c)
@@ -330,8 +365,8 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
   };
   // Interior KV tiles (every key visible to every row of the tile) and the diagonal tiles
   // are separate compile-time instantiations of the step: only the latter carry the mask.
-  const int n_full = static_cast<int>(
-      min(static_cast<long long>(n_kv), max(0LL, tile_limit + 1) / BN));
+  const int n_full = static_cast<int>(min(static_cast<long long>(n_kv),
+                                         max(0LL, (tile_limit + 1) / BN - k0)));
   int jj = 0;
   for (; jj < n_full; ++jj)
     if (!step(std::false_type{}, jj)) { ok = false; break; }
@@ -339,9 +374,46 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
     for (; jj < n_kv; ++jj)
       if (!step(std::true_type{}, jj)) { ok = false; break; }
 
+  const int row = q0 + r;
+  if (SPLIT && parts > 1) {
+    // Partial record of this row over this part: O and l relative to the running max m.
+    // Every lane takes part in the waits and TMEM loads (warp-collective); only the stores of
+    // rows past Tq are skipped. ok and n_kv are warp-uniform.
+    if (!ok) return;
+    float4* dst = reinterpret_cast<float4*>(part_record(p, bh, qb, part, t * BM + r));
+    const bool store = row < p.Tq;
+    if (n_kv == 0) {
+      // No KV tile of this part is visible to the tile: an empty record.
+      if (store) {
+#pragma unroll
+        for (int i = 0; i < HD / 4; ++i) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        dst[HD / 4] = make_float4(-INFINITY, 0.f, 0.f, 0.f);
+      }
+      return;
+    }
+    if (!warp_wait(s, &s.o_done[t], (n_kv - 1) & 1)) return;
+    tc_fence_after();
+    uint32_t o[HD / 32][32];
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + c * 32, o[c]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) reg_fence(o[c]);
+    if (store) {
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[c * 8 + i] =
+              make_float4(__uint_as_float(o[c][4 * i]), __uint_as_float(o[c][4 * i + 1]),
+                          __uint_as_float(o[c][4 * i + 2]), __uint_as_float(o[c][4 * i + 3]));
+      }
+      dst[HD / 4] = make_float4(m_run, l_run, 0.f, 0.f);
+    }
+    return;
+  }
   if (ok && n_kv > 0 && warp_wait(s, &s.o_done[t], (n_kv - 1) & 1)) {
     tc_fence_after();
-    const int row = q0 + r;
     const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
     uint32_t o[HD / 32][32];
 #pragma unroll
@@ -370,6 +442,9 @@ __device__ __forceinline__ void softmax_tile(Smem& s, const Params& p, uint32_t 
   }
 }
 
+// SPLIT: the KV split of few, long query blocks (a separate instantiation, so the common
+// unsplit kernel carries none of its bookkeeping).
+template <bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
 attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -380,10 +455,25 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Heaviest causal blocks first: blocks are dispatched roughly in index order.
+  // Heaviest causal blocks first: blocks are dispatched roughly in index order. With a KV
+  // split, CTA i is part i / BH of the block's parts (per block, from the heaviest block down).
   const int BH = p.B * p.H;
-  const int qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = static_cast<int>(blockIdx.x % BH);
+  int qb, bh, part = 0, parts = 1;
+  if (!SPLIT) {
+    qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.x / BH);
+    bh = static_cast<int>(blockIdx.x % BH);
+  } else {
+    int idx = static_cast<int>(blockIdx.x);
+    qb = p.n_qblocks - 1;
+    for (; qb > 0; --qb) {
+      const int np = block_parts(p, qb);
+      if (idx < np * BH) break;
+      idx -= np * BH;
+    }
+    parts = block_parts(p, qb);
+    part = idx / BH;
+    bh = idx - part * BH;
+  }
   const int b = bh / p.H;
   const int h = bh % p.H;
   int q0[TILES], n_kv[TILES];
@@ -393,7 +483,15 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
     n_kv[t] = kv_tiles_for(p, q0[t]);
   }
   // Tile 1 never needs fewer KV tiles than tile 0 unless it lies past Tq (then it needs none).
-  const int n_load = max(n_kv[0], n_kv[1]);
+  // This CTA's KV tiles [k0, k0 + n_load); per query tile, the steps it takes among them.
+  int k0 = 0;
+  int n_load = max(n_kv[0], n_kv[1]);
+  if constexpr (SPLIT) {
+    k0 = part * n_load / parts;
+    n_load = (part + 1) * n_load / parts - k0;
+#pragma unroll
+    for (int t = 0; t < TILES; ++t) n_kv[t] = max(0, min(n_kv[t] - k0, n_load));
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
@@ -435,7 +533,7 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
     regs_decrease<PRODUCER_REGS>();
     if (warp == LOAD_WARP && lane == 0) {
       int issued_k = 0, issued_v = 0;  // K / V tiles whose loads were issued
-      const int q_tiles = n_kv[1] > 0 ? 2 : 1;
+      const int q_tiles = q0[1] < p.Tq ? 2 : 1;
       mbar_arrive_expect_tx(&s.q_full, q_tiles * TILE_BYTES);
       for (int t = 0; t < q_tiles; ++t) tma_load_4d(s.q[t], &tm_q, &s.q_full, 0, q0[t], h, b);
       for (int j = 0; j < n_load; ++j) {
@@ -443,11 +541,11 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
         const uint32_t use = j / STAGES;
         if (j >= STAGES && !wait_or_abort(s, &s.k_empty[st], (use - 1) & 1)) break;
         mbar_arrive_expect_tx(&s.k_full[st], TILE_BYTES);
-        tma_load_4d(s.k[st], &tm_k, &s.k_full[st], 0, j * BN, h, b);
+        tma_load_4d(s.k[st], &tm_k, &s.k_full[st], 0, (k0 + j) * BN, h, b);
         issued_k = j + 1;
         if (j >= STAGES && !wait_or_abort(s, &s.v_empty[st], (use - 1) & 1)) break;
         mbar_arrive_expect_tx(&s.v_full[st], TILE_BYTES);
-        tma_load_4d(s.v[st], &tm_v, &s.v_full[st], 0, j * BN, h, b);
+        tma_load_4d(s.v[st], &tm_v, &s.v_full[st], 0, (k0 + j) * BN, h, b);
         issued_v = j + 1;
       }
       if (s.abort) {
@@ -523,7 +621,8 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
   } else {
     regs_increase<SOFTMAX_REGS>();
     const int t = warp / 4;
-    softmax_tile(s, p, tmem, t, warp % 4, lane, bh, q0[t], n_kv[0], n_kv[1]);
+    softmax_tile<SPLIT>(s, p, tmem, t, warp % 4, lane, bh, qb, q0[t], n_kv[0], n_kv[1], k0, part,
+                        parts);
   }
 
   tc_fence_before();
@@ -533,6 +632,57 @@ attention_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+}
+
+// Merge of the partial records of split query blocks: one warp per query row of the split
+// blocks (qb >= first_split_qb), lane i owns output features 2i, 2i + 1; lane q also reads part
+// q's running max and row sum (at most 32 parts), so the parts' records are fetched in
+// parallel. The parts' sums are weighted by exp2(m_part - M) (never averaged outputs);
+// O = sum / l, LSE in natural log.
+constexpr int COMBINE_WARPS = 8;
+
+__global__ void __launch_bounds__(COMBINE_WARPS * 32)
+prefill_combine_kernel(const Params p) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split_blocks = p.n_qblocks - p.first_split_qb;
+  const long long g = static_cast<long long>(blockIdx.x) * COMBINE_WARPS + warp;
+  const int row_in_block = static_cast<int>(g % BLOCK_M);
+  const long long blk = g / BLOCK_M;  // over (bh, split block)
+  const int qb = p.first_split_qb + static_cast<int>(blk % split_blocks);
+  const int bh = static_cast<int>(blk / split_blocks);
+  if (bh >= p.B * p.H) return;  // warp-uniform, as are the two exits below
+  const int row = qb * BLOCK_M + row_in_block;
+  if (row >= p.Tq) return;
+  const int parts = block_parts(p, qb);
+  if (parts <= 1) return;
+  const float* rec0 = part_record(p, bh, qb, 0, row_in_block);
+  const size_t stride = static_cast<size_t>(BLOCK_M) * PART_REC;
+  float mq = -INFINITY, lq = 0.f;
+  if (lane < parts) {
+    const float2 ml = *reinterpret_cast<const float2*>(rec0 + lane * stride + HD);
+    mq = ml.x;
+    lq = ml.y;
+  }
+  float M = mq;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  const float w = (mq == -INFINITY) ? 0.f : ex2_approx(mq - M);
+  float den = w * lq;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  float n0 = 0.f, n1 = 0.f;
+#pragma unroll 4
+  for (int q = 0; q < parts; ++q) {
+    const float wq = __shfl_sync(0xffffffffu, w, q);
+    const float2 a = reinterpret_cast<const float2*>(rec0 + q * stride)[lane];
+    n0 = fmaf(wq, a.x, n0);
+    n1 = fmaf(wq, a.y, n1);
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const size_t orow = static_cast<size_t>(bh) * p.Tq + row;
+  reinterpret_cast<uint32_t*>(p.o + orow * HD)[lane] = pack_bf16x2(n0 * inv, n1 * inv);
+  if (lane == 0) p.lse[orow] = den > 0.f ? (M + log2f(den)) * LN2 : -INFINITY;
 }
 
 }  // namespace prefill

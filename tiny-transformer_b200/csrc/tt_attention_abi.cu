@@ -84,6 +84,68 @@ bool use_direct_decode(int64_t bh, int64_t kv_len) {
   return kv_len <= kDirectDecodeMaxKeys && bh * kv_len <= kDirectDecodeMaxRows;
 }
 
+// Prefill work plan (shape only, so the workspace size never depends on the device). A CTA
+// computes one 256-row query block over its causal KV range, heaviest blocks first. When the
+// grid has fewer blocks than a 148-SM part has SMs, the longest block's KV loop sets the
+// kernel time (one long sequence, or few (batch x head) rows per GPU). The plan then splits
+// blocks longer than part_tiles into near-equal parts (separate CTAs, merged by
+// prefill_combine_kernel), with the smallest part_tiles (at least 4 KV tiles) whose CTAs
+// still fit one wave of 148. With more blocks than SMs no split is made: a second wave of
+// short CTAs measured slower than the unsplit grid (each CTA's prologue and epilogue cost
+// about three KV steps, and the combine kernel two).
+constexpr int64_t kPlanSms = 148;
+constexpr int64_t kMinPartTiles = 4;
+constexpr int kMaxParts = 32;  // prefill_combine_kernel reads one part per lane
+
+struct PrefillPlan {
+  int part_tiles = 0;  // 0: no split
+  int max_parts = 1;
+  int first_split_qb = 0;
+  int64_t ctas = 0;
+};
+
+int64_t host_kv_tiles(int64_t tq, int64_t tk, int64_t past, int64_t q0) {
+  if (q0 >= tq) return 0;
+  const int64_t end = std::min(tk, q0 + tt::prefill::BM + past);
+  return (end + tt::prefill::BN - 1) / tt::prefill::BN;
+}
+
+int64_t host_block_tiles(int64_t tq, int64_t tk, int64_t past, int64_t qb) {
+  const int64_t q0 = qb * tt::prefill::BLOCK_M;
+  return std::max(host_kv_tiles(tq, tk, past, q0),
+                  host_kv_tiles(tq, tk, past, q0 + tt::prefill::BM));
+}
+
+PrefillPlan prefill_plan(int64_t bh, int64_t tq, int64_t tk, int64_t past) {
+  PrefillPlan pl;
+  const int64_t nqb = (tq + tt::prefill::BLOCK_M - 1) / tt::prefill::BLOCK_M;
+  pl.ctas = bh * nqb;
+  if (pl.ctas >= kPlanSms) return pl;
+  const int64_t longest = host_block_tiles(tq, tk, past, nqb - 1);  // never decreases with qb
+  for (int64_t part = kMinPartTiles; part < longest; ++part) {
+    if ((longest + part - 1) / part > kMaxParts) continue;
+    int64_t ctas = 0;
+    for (int64_t qb = 0; qb < nqb; ++qb)
+      ctas += std::max<int64_t>(1, (host_block_tiles(tq, tk, past, qb) + part - 1) / part);
+    if (ctas * bh > kPlanSms) continue;
+    pl.part_tiles = static_cast<int>(part);
+    pl.max_parts = static_cast<int>((longest + part - 1) / part);
+    pl.ctas = ctas * bh;
+    pl.first_split_qb = static_cast<int>(nqb);
+    for (int64_t qb = nqb - 1; qb >= 0 && host_block_tiles(tq, tk, past, qb) > part; --qb)
+      pl.first_split_qb = static_cast<int>(qb);
+    return pl;
+  }
+  return pl;  // no part size fits one wave (or the blocks are already short): no split
+}
+
+size_t prefill_workspace_bytes(int64_t bh, int64_t tq, const PrefillPlan& pl) {
+  if (pl.part_tiles == 0) return 0;
+  const int64_t nqb = (tq + tt::prefill::BLOCK_M - 1) / tt::prefill::BLOCK_M;
+  return static_cast<size_t>(bh * nqb * pl.max_parts) * tt::prefill::BLOCK_M *
+         tt::prefill::PART_REC * sizeof(float);
+}
+
 // Bytes of the per-sequence arrival counters of a split decode (one unsigned per (batch, head),
 // rounded up to 256 bytes so the partials after them stay aligned).
 size_t decode_arrival_bytes(int64_t bh) {
@@ -219,23 +281,29 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
   if (!ds.attrs_set) {
     // The prefill kernel hands registers between warpgroups (setmaxnreg); that is only
     // sound when it launches with exactly the register count the hand-over was sized for.
-    const void* prefill_fn = reinterpret_cast<const void*>(tt::prefill::attention_prefill_kernel);
+    const void* prefill_fns[2] = {
+        reinterpret_cast<const void*>(tt::prefill::attention_prefill_kernel<false>),
+        reinterpret_cast<const void*>(tt::prefill::attention_prefill_kernel<true>)};
     const unsigned launch_regs = tt::prefill::LAUNCH_REGS;
     const int prefill_smem = static_cast<int>(tt::prefill::kSmemBytes);
-    cudaFuncAttributes fa{};
-    e = cudaFuncGetAttributes(&fa, prefill_fn);
-    if (e != cudaSuccess)
-      return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaFuncGetAttributes: ") + cudaGetErrorString(e));
-    if (fa.numRegs != static_cast<int>(launch_regs)) {
-      char buf[160];
-      std::snprintf(buf, sizeof(buf),
-                    "prefill kernel was compiled with %d registers per thread, expected %u; "
-                    "rebuild libtt_attention.so",
-                    fa.numRegs, launch_regs);
-      return fail(TT_ATTN_UNSUPPORTED, buf);
+    for (const void* prefill_fn : prefill_fns) {
+      cudaFuncAttributes fa{};
+      e = cudaFuncGetAttributes(&fa, prefill_fn);
+      if (e != cudaSuccess)
+        return fail(TT_ATTN_LAUNCH_FAIL,
+                    std::string("cudaFuncGetAttributes: ") + cudaGetErrorString(e));
+      if (fa.numRegs != static_cast<int>(launch_regs)) {
+        char buf[160];
+        std::snprintf(buf, sizeof(buf),
+                      "prefill kernel was compiled with %d registers per thread, expected %u; "
+                      "rebuild libtt_attention.so",
+                      fa.numRegs, launch_regs);
+        return fail(TT_ATTN_UNSUPPORTED, buf);
+      }
+      e = cudaFuncSetAttribute(prefill_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               prefill_smem);
+      if (e != cudaSuccess) break;
     }
-    e = cudaFuncSetAttribute(prefill_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             prefill_smem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -293,8 +361,15 @@ TT_ATTN_API int tt_attn_layout_supported(const void* ptr, const int64_t* strides
 
 TT_ATTN_API size_t tt_attn_forward_workspace_size(int64_t batch, int64_t heads, int64_t q_len,
                                                   int64_t kv_len) {
-  if (batch <= 0 || heads <= 0 || q_len != 1 || kv_len <= 0 || kv_len > INT32_MAX) return 0;
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0 || kv_len > INT32_MAX ||
+      q_len > kv_len)
+    return 0;
   if (batch > INT32_MAX / heads) return 0;
+  if (q_len > 1) {
+    // Prefill: partial records of split query blocks (causal, past_len = kv_len - q_len).
+    const int64_t bh = batch * heads;
+    return prefill_workspace_bytes(bh, q_len, prefill_plan(bh, q_len, kv_len, kv_len - q_len));
+  }
   // Short and medium caches take the cluster kernel, which needs no workspace.
   if (use_direct_decode(batch * heads, kv_len)) return 0;
   const int64_t bh = batch * heads;
@@ -654,7 +729,7 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     const int64_t n_qblocks = (q_len + tt::prefill::BLOCK_M - 1) / tt::prefill::BLOCK_M;
     if (n_qblocks > INT32_MAX / bh)
       return fail(TT_ATTN_BAD_ARG, "attention shape exceeds the supported CUDA grid limits");
-    grid = bh * n_qblocks;
+    grid = bh * n_qblocks;  // without a KV split; with one, at most 2 x 148 + the parts
   }
 
   const Shape4 qs = canonical(batch, heads, q_len, q_strides);
@@ -767,6 +842,7 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
   if (!encode_map(&tmq, q, qs, &err) || !encode_map(&tmk, k, ks, &err, kv_box) ||
       !encode_map(&tmv, v, vs, &err, kv_box))
     return fail(TT_ATTN_UNSUPPORTED, err);
+  const PrefillPlan plan = prefill_plan(bh, q_len, kv_len, past_len);
   tt::prefill::Params p{};
   p.B = static_cast<int>(batch);
   p.H = static_cast<int>(heads);
@@ -777,9 +853,25 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
   p.o = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
   p.scale_log2 = kScaleLog2;
-  tt::prefill::attention_prefill_kernel<<<static_cast<unsigned>(grid), tt::prefill::THREADS,
-                                          tt::prefill::kSmemBytes, cs>>>(tmq, tmk, tmv, p);
-  return check_launch("attention_prefill_kernel launch");
+  p.part_tiles = plan.part_tiles;
+  p.max_parts = plan.max_parts;
+  p.first_split_qb = plan.first_split_qb;
+  p.partials = static_cast<float*>(workspace);
+  if (plan.part_tiles == 0) {
+    tt::prefill::attention_prefill_kernel<false>
+        <<<static_cast<unsigned>(plan.ctas), tt::prefill::THREADS, tt::prefill::kSmemBytes, cs>>>(
+            tmq, tmk, tmv, p);
+    return check_launch("attention_prefill_kernel launch");
+  }
+  tt::prefill::attention_prefill_kernel<true>
+      <<<static_cast<unsigned>(plan.ctas), tt::prefill::THREADS, tt::prefill::kSmemBytes, cs>>>(
+          tmq, tmk, tmv, p);
+  if ((st = check_launch("attention_prefill_kernel launch")) != TT_ATTN_OK) return st;
+  const int64_t rows = bh * (p.n_qblocks - plan.first_split_qb) * tt::prefill::BLOCK_M;
+  const int64_t blocks = (rows + tt::prefill::COMBINE_WARPS - 1) / tt::prefill::COMBINE_WARPS;
+  tt::prefill::prefill_combine_kernel<<<static_cast<unsigned>(blocks),
+                                        tt::prefill::COMBINE_WARPS * 32, 0, cs>>>(p);
+  return check_launch("prefill_combine_kernel launch");
 }
 
 }  // extern "C"
