@@ -137,6 +137,12 @@ def sharded_attention(q, k, v, past_len: int = 0, kv_lens: torch.Tensor | None =
     o, lse, shard, axis = run_sharded(compute, q, k, v, past_len, rank, world, kv_lens)
     if not gather:
         return o, lse, shard, axis
+    if world == 1:
+        # The one shard is the whole problem: no collective.
+        if axis == "bh":
+            B, H, Tq, D = q.shape
+            return o.reshape(B, H, Tq, D), lse.reshape(B, H, Tq)
+        return o, lse
     if axis == "batch":
         lens = kv_lens.tolist() if kv_lens is not None else [k.shape[2]] * q.shape[0]
         sizes = [s.size for s in balanced_batch_shards(lens, world)]
