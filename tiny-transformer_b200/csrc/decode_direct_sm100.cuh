@@ -103,44 +103,55 @@ decode_direct_kernel(const Params p) {
   const int rank = static_cast<int>(cluster_ctarank());
   const int bh = static_cast<int>(blockIdx.x) / p.splits;
   const int b = bh / p.H, h = bh - b * p.H;
+  // The q pair this thread stages (threads 0-31) and the sequence length are requested first;
+  // the first pass's K and V rows are requested before q is staged in shared memory, so the
+  // q round trip overlaps the K/V one.
+  uint32_t qpair = 0;
+  if (threadIdx.x < HD / 2)
+    qpair = __ldg(reinterpret_cast<const uint32_t*>(p.q + b * p.q_sb + h * p.q_sh) + threadIdx.x);
   int L = p.Tk;
-  if (p.kv_lens != nullptr) L = min(max(p.kv_lens[b], 0), p.Tk);
+  if (p.kv_lens != nullptr) L = min(max(__ldg(p.kv_lens + b), 0), p.Tk);
   const int k_begin = rank * p.keys_per_cta;
   const int k_end = min(L, k_begin + p.keys_per_cta);
-
-  // q * scale * log2(e) in shared memory (FP32); every lane reads it as broadcasts.
-  if (threadIdx.x < HD / 2) {
-    const uint32_t pair =
-        reinterpret_cast<const uint32_t*>(p.q + b * p.q_sb + h * p.q_sh)[threadIdx.x];
-    qs[2 * threadIdx.x] = bf16_lo(pair) * p.scale_log2;
-    qs[2 * threadIdx.x + 1] = bf16_hi(pair) * p.scale_log2;
-  }
-  __syncthreads();
-  const uint32_t qaddr = smem_u32(qs);
   const __nv_bfloat16* kb = p.k + b * p.k_sb + h * p.k_sh;
   const __nv_bfloat16* vb = p.v + b * p.v_sb + h * p.v_sh;
   // Row stride of V in bf16 pairs (strides are multiples of 8 elements; a row step fits int).
   const int v_pairs = static_cast<int>(p.v_st >> 1);
 
-  float m = -INFINITY;       // warp-uniform running max (log2 units)
-  float l = 0.f;             // this lane's share of the running sum
-  float a0 = 0.f, a1 = 0.f;  // output features 2*lane, 2*lane + 1
-  for (int base = k_begin + warp * 32; base < k_end; base += KEYS_PER_PASS) {
-    const int n_valid = min(32, k_end - base);  // warp-uniform
-    const int row = base + lane;
-    uint4 kr[8];
+  // Requests of one pass: this lane's K row and the pass's V row pairs (rows below n_valid).
+  auto load_pass = [&](int base, int n_valid, uint4 (&kr)[8], uint32_t (&vv)[32]) {
     if (lane < n_valid) {
-      const uint4* krow = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(row) * p.k_st);
+      const uint4* krow =
+          reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(base + lane) * p.k_st);
 #pragma unroll
       for (int c = 0; c < 8; ++c) kr[c] = __ldg(krow + c);
     }
-    // Row rr of the pass: this lane's two features at vrow + rr * v_pairs (u32 units).
     const uint32_t* vrow =
         reinterpret_cast<const uint32_t*>(vb + static_cast<int64_t>(base) * p.v_st) + lane;
-    uint32_t vv[32];
 #pragma unroll
     for (int rr = 0; rr < 32; ++rr)
       if (rr < n_valid) vv[rr] = __ldg(vrow + rr * v_pairs);
+  };
+
+  uint4 kr[8];
+  uint32_t vv[32];
+  int base = k_begin + warp * 32;
+  if (base < k_end) load_pass(base, min(32, k_end - base), kr, vv);
+
+  // q * scale * log2(e) in shared memory (FP32); every lane reads it as broadcasts.
+  if (threadIdx.x < HD / 2) {
+    qs[2 * threadIdx.x] = bf16_lo(qpair) * p.scale_log2;
+    qs[2 * threadIdx.x + 1] = bf16_hi(qpair) * p.scale_log2;
+  }
+  __syncthreads();
+  const uint32_t qaddr = smem_u32(qs);
+
+  float m = -INFINITY;       // warp-uniform running max (log2 units)
+  float l = 0.f;             // this lane's share of the running sum
+  float a0 = 0.f, a1 = 0.f;  // output features 2*lane, 2*lane + 1
+  for (; base < k_end; base += KEYS_PER_PASS) {
+    const int n_valid = min(32, k_end - base);  // warp-uniform
+    if (base != k_begin + warp * 32) load_pass(base, n_valid, kr, vv);
     float x = -INFINITY;
     if (lane < n_valid) {
       float d[4] = {0.f, 0.f, 0.f, 0.f};
