@@ -175,6 +175,27 @@ TT_ATTN_API tt_attn_status tt_rope_append_bf16(
     void* q_out, void* cache_k, const int64_t* ck_strides, void* cache_v,
     const int64_t* cv_strides, int64_t capacity, void* stream);
 
+/* QKV projection with RoPE and the KV-cache append in its epilogue, one kernel per layer: the
+ * steps in front of the attention in the reference's Block.forward (model.py:59-67:
+ * `linear(normalized, qkv)`, `rope(q)`, `rope(k)`, `KVCache.update`), with the projection never
+ * written to memory.
+ *   hidden   [batch * q_len, dim] bf16 row-major (the normalised hidden state), dim % 64 == 0
+ *   w_qkv    [3 * heads * 64, dim] bf16 row-major (the layer's qkv weight)
+ *   cos/sin  [table_len, 32] FP32 tables; position: first position (or position_dev, an int64
+ *            on the device read at run time)
+ *   q_out    [batch, heads, q_len, 64] bf16 contiguous = rope(q)
+ *   cache_k/cache_v [batch, heads, capacity, 64] bf16 (unit last stride): rows position + t get
+ *            rope(k) and v.
+ * The projection is accumulated in FP32 and rounded to bf16, then rotated exactly as
+ * tt_rope_append_bf16 rotates a bf16 projection. All pointers 16-byte aligned. The feature
+ * tile width (16 to 128 features) is chosen per call so that the grid covers the SMs; the
+ * result does not depend on it. */
+TT_ATTN_API tt_attn_status tt_qkv_rope_append_bf16(
+    const void* hidden, int64_t batch, int64_t q_len, int64_t dim, const void* w_qkv,
+    int64_t heads, const float* cos, const float* sin, int64_t table_len, int64_t position,
+    const int64_t* position_dev, void* q_out, void* cache_k, const int64_t* ck_strides,
+    void* cache_v, const int64_t* cv_strides, int64_t capacity, void* stream);
+
 /* Diagnostic for the failure path: launches one warp on `stream` that waits on a barrier
  * phase nothing completes, bounded by `budget_cycles` (1 .. 1e9 SM clock cycles). The wait
  * gives up by itself and sets bit 0 of the device status, which the caller then reads (and

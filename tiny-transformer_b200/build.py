@@ -33,7 +33,7 @@ GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 KERNEL_SOURCES = ["tt_attention_abi.cu"]
 KERNEL_HEADERS = ["sm100_ptx.cuh", "prefill_sm100.cuh", "decode_sm100.cuh",
                   "decode_direct_sm100.cuh",
-                  "rope_append_sm100.cuh", "selftest_sm100.cuh", "backward_sm100.cuh",
+                  "rope_append_sm100.cuh", "qkv_rope_sm100.cuh", "selftest_sm100.cuh", "backward_sm100.cuh",
                   "backward_det_sm100.cuh"]
 
 

@@ -96,6 +96,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// 2-D tiled tensor load (no multicast) into CTA shared memory; completion is signalled on
+// `bar` as transaction bytes. c0 is the innermost coordinate.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1),
+        "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 4-D tiled tensor reduce-add from CTA shared memory into global memory (element type and
 // swizzle from the tensor map; elements outside the tensor are skipped). Tracked by the
 // issuing thread's bulk async-group.

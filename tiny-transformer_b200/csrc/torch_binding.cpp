@@ -268,6 +268,67 @@ torch::Tensor rope_append(const torch::Tensor& qkv, const torch::Tensor& cos,
   return q_out;
 }
 
+// QKV projection + RoPE + KV-cache append in one kernel (tt_qkv_rope_append_bf16). `hidden`
+// is the normalised hidden state [B, T, dim]; `w_qkv` the layer's [3 * H * 64, dim] weight;
+// `position` as for rope_append.
+torch::Tensor qkv_rope_append(const torch::Tensor& hidden, const torch::Tensor& w_qkv,
+                              const torch::Tensor& cos, const torch::Tensor& sin,
+                              const pybind11::object& position, torch::Tensor cache_k,
+                              torch::Tensor cache_v) {
+  for (const torch::Tensor* t : {&hidden, &w_qkv, &cos, &sin,
+                                 static_cast<const torch::Tensor*>(&cache_k),
+                                 static_cast<const torch::Tensor*>(&cache_v)}) {
+    TORCH_CHECK(t->is_cuda(), "qkv_rope_append: all tensors must be CUDA tensors");
+    TORCH_CHECK(t->device() == hidden.device(),
+                "qkv_rope_append: all tensors must be on the same device");
+  }
+  TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 && w_qkv.scalar_type() == at::kBFloat16 &&
+                  cache_k.scalar_type() == at::kBFloat16 && cache_v.scalar_type() == at::kBFloat16,
+              "qkv_rope_append: hidden, w_qkv and the caches must be bf16");
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat,
+              "qkv_rope_append: cos/sin tables must be float32");
+  TORCH_CHECK(hidden.dim() == 3 && hidden.is_contiguous(),
+              "qkv_rope_append: hidden must be a contiguous [B, T, dim] tensor");
+  const int64_t B = hidden.size(0), T = hidden.size(1), dim = hidden.size(2);
+  TORCH_CHECK(w_qkv.dim() == 2 && w_qkv.is_contiguous() && w_qkv.size(1) == dim &&
+                  w_qkv.size(0) % (3 * TT_ATTN_HEAD_DIM) == 0,
+              "qkv_rope_append: w_qkv must be a contiguous [3 * H * 64, dim] weight");
+  const int64_t H = w_qkv.size(0) / (3 * TT_ATTN_HEAD_DIM);
+  TORCH_CHECK(cos.dim() == 2 && cos.size(1) == TT_ATTN_HEAD_DIM / 2 && cos.is_contiguous() &&
+                  sin.sizes() == cos.sizes() && sin.is_contiguous(),
+              "qkv_rope_append: cos/sin must be contiguous [L, 32] tables");
+  for (const torch::Tensor* c : {&cache_k, &cache_v})
+    TORCH_CHECK(c->dim() == 4 && c->size(0) == B && c->size(1) == H &&
+                    c->size(3) == TT_ATTN_HEAD_DIM && c->stride(3) == 1,
+                "qkv_rope_append: caches must be [B, H, capacity, 64] with contiguous rows");
+  TORCH_CHECK(cache_v.size(2) == cache_k.size(2),
+              "qkv_rope_append: caches must have equal capacity");
+  int64_t pos = 0;
+  const int64_t* pos_dev = nullptr;
+  torch::Tensor pos_t;
+  if (pybind11::isinstance<pybind11::int_>(position)) {
+    pos = position.cast<int64_t>();
+  } else {
+    pos_t = position.cast<torch::Tensor>();
+    TORCH_CHECK(pos_t.is_cuda() && pos_t.device() == hidden.device() &&
+                    pos_t.scalar_type() == at::kLong && pos_t.numel() == 1,
+                "qkv_rope_append: a tensor position must be a one-element int64 CUDA tensor");
+    pos_dev = pos_t.data_ptr<int64_t>();
+  }
+  const c10::cuda::CUDAGuard device_guard(hidden.device());
+  auto q_out = torch::empty({B, H, T, TT_ATTN_HEAD_DIM}, hidden.options());
+  const int64_t ks[4] = {cache_k.stride(0), cache_k.stride(1), cache_k.stride(2), 1};
+  const int64_t vs[4] = {cache_v.stride(0), cache_v.stride(1), cache_v.stride(2), 1};
+  auto stream = c10::cuda::getCurrentCUDAStream(hidden.get_device());
+  const tt_attn_status st = tt_qkv_rope_append_bf16(
+      hidden.data_ptr(), B, T, dim, w_qkv.data_ptr(), H, cos.data_ptr<float>(),
+      sin.data_ptr<float>(), cos.size(0), pos, pos_dev, q_out.data_ptr(), cache_k.data_ptr(), ks,
+      cache_v.data_ptr(), vs, cache_k.size(2), static_cast<void*>(stream.stream()));
+  TORCH_CHECK(st == TT_ATTN_OK, "tt_qkv_rope_append_bf16 failed: ", tt_attn_status_string(st),
+              ": ", tt_attn_last_error());
+  return q_out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_forward", &attention_forward,
         "BF16 causal attention forward on sm_100a (returns O and natural-log FP32 LSE)",
@@ -283,6 +344,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Fused RoPE on q/k of a [B, T, 3, H, 64] QKV projection + KV-cache append; returns rope(q)",
         pybind11::arg("qkv"), pybind11::arg("cos"), pybind11::arg("sin"),
         pybind11::arg("position"), pybind11::arg("cache_k"), pybind11::arg("cache_v"));
+  m.def("qkv_rope_append", &qkv_rope_append,
+        "QKV projection + RoPE on q/k + KV-cache append in one kernel; returns rope(q)",
+        pybind11::arg("hidden"), pybind11::arg("w_qkv"), pybind11::arg("cos"),
+        pybind11::arg("sin"), pybind11::arg("position"), pybind11::arg("cache_k"),
+        pybind11::arg("cache_v"));
   m.attr("HEAD_DIM") = TT_ATTN_HEAD_DIM;
   m.attr("ABI_VERSION") = TT_ATTN_ABI_VERSION;
 }

@@ -21,6 +21,7 @@
 #include "decode_direct_sm100.cuh"
 #include "selftest_sm100.cuh"
 #include "rope_append_sm100.cuh"
+#include "qkv_rope_sm100.cuh"
 #include "backward_sm100.cuh"
 #include "backward_det_sm100.cuh"
 
@@ -229,6 +230,61 @@ bool encode_map_f32(CUtensorMap* map, void* base, const Shape4& s, std::string* 
   return true;
 }
 
+// 2-D map over a row-major [rows, cols] bf16 matrix (dims innermost first), box 64 x 128,
+// 128-byte swizzle; rows past `rows` read as zero. cols * 2 must be a multiple of 16 bytes.
+bool encode_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                   uint32_t box_rows, std::string* err) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
+    return false;
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    *err = buf;
+    return false;
+  }
+  return true;
+}
+
+template <int BN>
+cudaError_t set_qkv_rope_attribute() {
+  return cudaFuncSetAttribute(tt::qkv_rope::qkv_rope_append_kernel<BN>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(tt::qkv_rope::smem_bytes<BN>()));
+}
+
+// Feature-tile width of the fused QKV kernel: the widest of 128, 64, 32, 16 whose grid covers
+// at least 85 % of the SMs (one CTA per SM fits), else 16. 128-feature tiles span two heads, so
+// they need an even head count to stay inside one of q, k, v.
+int qkv_rope_tile_width(int64_t rows, int64_t heads, int sms) {
+  const int64_t m_tiles = (rows + tt::qkv_rope::BM - 1) / tt::qkv_rope::BM;
+  const int64_t n = 3 * heads * TT_ATTN_HEAD_DIM;
+  const int64_t want = (static_cast<int64_t>(sms > 0 ? sms : 148) * 85 + 99) / 100;
+  for (int bn : {128, 64, 32}) {
+    if (bn == 128 && heads % 2 != 0) continue;
+    if (m_tiles * (n / bn) >= want) return bn;
+  }
+  return 16;
+}
+
+template <int BN>
+void launch_qkv_rope(const CUtensorMap& tm_h, const CUtensorMap& tm_w, const tt::qkv_rope::Params& p,
+                     int64_t n, int64_t m_tiles, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>(n / BN), static_cast<unsigned>(m_tiles));
+  tt::qkv_rope::qkv_rope_append_kernel<BN>
+      <<<grid, tt::qkv_rope::THREADS, tt::qkv_rope::smem_bytes<BN>(), stream>>>(tm_h, tm_w, p);
+}
+
 // ------------------------------------------------------------------ per-device setup
 struct DeviceState {
   bool checked = false;
@@ -304,6 +360,10 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
                                prefill_smem);
       if (e != cudaSuccess) break;
     }
+    if (e == cudaSuccess) e = set_qkv_rope_attribute<128>();
+    if (e == cudaSuccess) e = set_qkv_rope_attribute<64>();
+    if (e == cudaSuccess) e = set_qkv_rope_attribute<32>();
+    if (e == cudaSuccess) e = set_qkv_rope_attribute<16>();
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -456,6 +516,80 @@ TT_ATTN_API tt_attn_status tt_rope_append_bf16(
       static_cast<unsigned>((rows + tt::rope::ROWS_PER_BLOCK - 1) / tt::rope::ROWS_PER_BLOCK);
   tt::rope::rope_append_kernel<<<grid, tt::rope::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("rope_append_kernel launch");
+}
+
+TT_ATTN_API tt_attn_status tt_qkv_rope_append_bf16(
+    const void* hidden, int64_t batch, int64_t q_len, int64_t dim, const void* w_qkv,
+    int64_t heads, const float* cos, const float* sin, int64_t table_len, int64_t position,
+    const int64_t* position_dev, void* q_out, void* cache_k, const int64_t* ck_strides,
+    void* cache_v, const int64_t* cv_strides, int64_t capacity, void* stream) {
+  namespace qr = tt::qkv_rope;
+  if (!hidden || !w_qkv || !cos || !sin || !q_out || !cache_k || !cache_v || !ck_strides ||
+      !cv_strides)
+    return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: pointers must not be NULL");
+  if (batch <= 0 || q_len <= 0 || heads <= 0 || dim <= 0 || capacity <= 0 || table_len <= 0)
+    return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: sizes must be positive");
+  if (dim % qr::BK != 0)
+    return fail(TT_ATTN_UNSUPPORTED, "qkv_rope_append: the input dimension must be a multiple of 64");
+  if (batch > INT32_MAX / q_len || heads > INT32_MAX / (3 * TT_ATTN_HEAD_DIM) ||
+      dim > INT32_MAX)
+    return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: shape exceeds the supported grid");
+  if (ck_strides[3] != 1 || cv_strides[3] != 1)
+    return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: cache rows must be contiguous (last stride 1)");
+  for (int i = 0; i < 3; ++i)
+    if (ck_strides[i] % 8 != 0 || cv_strides[i] % 8 != 0)
+      return fail(TT_ATTN_BAD_ARG,
+                  "qkv_rope_append: cache strides must be multiples of 8 elements (16-byte rows)");
+  for (const void* ptr : {hidden, w_qkv, static_cast<const void*>(q_out),
+                          static_cast<const void*>(cache_k), static_cast<const void*>(cache_v),
+                          static_cast<const void*>(cos), static_cast<const void*>(sin)})
+    if (!aligned16(ptr))
+      return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: pointers must be 16-byte aligned");
+  if (position_dev == nullptr &&
+      (position < 0 || position + q_len > capacity || position + q_len > table_len))
+    return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: position + q_len exceeds the cache capacity "
+                                 "or the cos/sin table");
+  const int64_t rows = batch * q_len;
+  const int64_t n = 3 * heads * TT_ATTN_HEAD_DIM;
+  const int64_t m_tiles = (rows + qr::BM - 1) / qr::BM;
+  if (m_tiles > 65535) return fail(TT_ATTN_BAD_ARG, "qkv_rope_append: too many rows for the grid");
+  int dev = 0, sm_count = 0;
+  tt_attn_status st = prepare_device(&dev, &sm_count);
+  if (st != TT_ATTN_OK) return st;
+  const int bn = qkv_rope_tile_width(rows, heads, sm_count);
+  // One row tile: the h box covers only the rows that exist (TMA fills past M with zeros).
+  const uint32_t box_rows = m_tiles == 1 ? static_cast<uint32_t>((rows + 7) / 8 * 8)
+                                         : static_cast<uint32_t>(qr::BM);
+  CUtensorMap tm_h, tm_w;
+  std::string err;
+  if (!encode_map_2d(&tm_h, hidden, rows, dim, box_rows, &err) ||
+      !encode_map_2d(&tm_w, w_qkv, n, dim, static_cast<uint32_t>(bn), &err))
+    return fail(TT_ATTN_UNSUPPORTED, err);
+  qr::Params p{};
+  p.M = static_cast<int>(rows);
+  p.T = static_cast<int>(q_len);
+  p.H = static_cast<int>(heads);
+  p.K = static_cast<int>(dim);
+  p.cos = cos;
+  p.sin = sin;
+  p.table_len = table_len;
+  p.position = position;
+  p.position_dev = reinterpret_cast<const long long*>(position_dev);
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.cache_k = static_cast<__nv_bfloat16*>(cache_k);
+  p.cache_v = static_cast<__nv_bfloat16*>(cache_v);
+  p.ck_s0 = ck_strides[0]; p.ck_s1 = ck_strides[1]; p.ck_s2 = ck_strides[2];
+  p.cv_s0 = cv_strides[0]; p.cv_s1 = cv_strides[1]; p.cv_s2 = cv_strides[2];
+  p.capacity = capacity;
+  p.stage_tx_bytes = (box_rows + static_cast<uint32_t>(bn)) * qr::BK * 2;
+  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 128: launch_qkv_rope<128>(tm_h, tm_w, p, n, m_tiles, cs); break;
+    case 64: launch_qkv_rope<64>(tm_h, tm_w, p, n, m_tiles, cs); break;
+    case 32: launch_qkv_rope<32>(tm_h, tm_w, p, n, m_tiles, cs); break;
+    default: launch_qkv_rope<16>(tm_h, tm_w, p, n, m_tiles, cs); break;
+  }
+  return check_launch("qkv_rope_append_kernel launch");
 }
 
 // Backward workspace: -LSE * log2(e) and -D per query row, each [B, H, Tq_pad] FP32 with Tq

@@ -17,8 +17,11 @@ Two decode paths:
   logits, argmax, position advance) captured once in a CUDA graph.
 
 With the student attention and a cache, RoPE on q/k and the K/V append run as one kernel per
-layer (``operators.fused.rope_append``) reading FP32 cos/sin tables built once per model, in
-place of the reference's ~20 elementwise launches for ``rope`` and ``KVCache.update``. Attention reads the
+layer reading FP32 cos/sin tables built once per model, in place of the reference's ~20
+elementwise launches for ``rope`` and ``KVCache.update``: inside the QKV projection's epilogue
+(``operators.fused.qkv_rope_append``, the projection never written to memory) when the width
+is a multiple of 64, else after the cuBLAS projection
+(``operators.fused.rope_append``). Attention reads the
   full-capacity cache with per-sequence lengths ``kv_lens`` held on the device, so the same
   graph serves every step and the host only replays it.
 
@@ -217,15 +220,27 @@ class Block(nn.Module):
         h = rms_norm(x, self.attn_norm, cfg.norm_eps)
         return F.linear(h, self.qkv).view(batch, time, 3, cfg.n_heads, cfg.head_dim)
 
-    def forward_fused(self, x, tables, layer, cache, position, kv_lens=None):
+    def forward_fused(self, x, tables, layer, cache, position, kv_lens=None, fused_qkv=False):
         """Student path: one kernel applies RoPE to q/k and appends k/v to the cache
         (operators.fused.rope_append), then attention reads the cache in place. With
-        ``kv_lens`` (captured decode) attention sees the full-capacity cache masked per
-        sequence; otherwise the live prefix [0, position + T)."""
+        ``fused_qkv`` the QKV projection itself runs in that kernel too (its epilogue applies
+        RoPE and writes the cache rows; the projection never reaches memory). With ``kv_lens``
+        (captured decode) attention sees the full-capacity cache masked per sequence;
+        otherwise the live prefix [0, position + T)."""
         from .operators import fused, student
-        qkv = self.qkv_rows(x)
-        keys, values = cache.storage_for(layer, qkv)
-        q = fused.rope_append(qkv, tables[0], tables[1], position, keys, values)
+        cfg = self.config
+        if fused_qkv:
+            batch = x.shape[0]
+            if batch != cache.batch_size:
+                raise ValueError("KV cache capacity exceeded or batch size changed")
+            h = rms_norm(x, self.attn_norm, cfg.norm_eps).contiguous()
+            proto = h.new_empty((batch, cfg.n_heads, 1, cfg.head_dim))
+            keys, values = cache._storage(layer, proto, proto)
+            q = fused.qkv_rope_append(h, self.qkv, tables[0], tables[1], position, keys, values)
+        else:
+            qkv = self.qkv_rows(x)
+            keys, values = cache.storage_for(layer, qkv)
+            q = fused.rope_append(qkv, tables[0], tables[1], position, keys, values)
         if kv_lens is not None:
             attended = student.attention(q, keys, values, cache.capacity - 1, None, kv_lens)
         else:
@@ -256,8 +271,10 @@ class Decoder(nn.Module):
         self.register_buffer("rope_cos", torch.empty(0), persistent=False)
         self.register_buffer("rope_sin", torch.empty(0), persistent=False)
         self._build_rope_tables()
-        # With the student attention, RoPE + cache append run as one fused kernel.
+        # With the student attention, RoPE + cache append run as one fused kernel, and (when
+        # the width is a multiple of 64) inside the QKV projection's epilogue.
         self.fused_rope = True
+        self.fused_qkv = config.dim % 64 == 0
 
     def _build_rope_tables(self):
         positions = torch.arange(self.config.max_seq_len, device=self.embedding.device)
@@ -311,7 +328,8 @@ class Decoder(nn.Module):
         if self.uses_fused(cache):
             tables = (self.rope_cos, self.rope_sin)
             for layer, block in enumerate(self.blocks):
-                x = block.forward_fused(x, tables, layer, cache, past_len)
+                x = block.forward_fused(x, tables, layer, cache, past_len,
+                                        fused_qkv=self.fused_qkv)
         else:
             cos, sin = self.rope_tables(torch.arange(past_len, past_len + time_, device=ids.device))
             for layer, block in enumerate(self.blocks):
@@ -374,7 +392,8 @@ class GraphedDecode:
         if model.fused_rope:
             tables = (model.rope_cos, model.rope_sin)
             for layer, block in enumerate(model.blocks):
-                x = block.forward_fused(x, tables, layer, cache, self.position, self.kv_lens)
+                x = block.forward_fused(x, tables, layer, cache, self.position, self.kv_lens,
+                                        fused_qkv=model.fused_qkv)
         else:
             cos, sin = model.rope_tables(self.position)
             for layer, block in enumerate(model.blocks):

@@ -68,6 +68,12 @@ def load_c_abi() -> ctypes.CDLL:
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_void_p, i64p, ctypes.c_void_p, i64p, ctypes.c_int64, ctypes.c_void_p]
+    lib.tt_qkv_rope_append_bf16.restype = ctypes.c_int
+    lib.tt_qkv_rope_append_bf16.argtypes = [
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, i64p, ctypes.c_void_p, i64p,
+        ctypes.c_int64, ctypes.c_void_p]
     lib.tt_attn_selftest_wait_timeout.restype = ctypes.c_int
     lib.tt_attn_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
     lib.tt_attn_status_string.restype = ctypes.c_char_p

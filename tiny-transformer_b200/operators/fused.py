@@ -14,3 +14,16 @@ def rope_append(qkv, cos, sin, position, cache_k, cache_v):
     (model.py:29-41).
     """
     return load_attention_extension().rope_append(qkv, cos, sin, position, cache_k, cache_v)
+
+
+def qkv_rope_append(hidden, w_qkv, cos, sin, position, cache_k, cache_v):
+    """The QKV projection of a decoder layer with RoPE and the KV-cache append in its epilogue.
+
+    ``hidden`` is the normalised hidden state ``[B, T, dim]`` (BF16, contiguous), ``w_qkv`` the
+    layer's ``[3 * H * 64, dim]`` weight (the reference's ``Block.qkv``). Equivalent to
+    ``rope_append(F.linear(hidden, w_qkv).view(B, T, 3, H, 64), ...)`` with the projection
+    accumulated in FP32 inside the kernel and never written to memory (model.py:59-67); returns
+    rope(q) as ``[B, H, T, 64]``.
+    """
+    return load_attention_extension().qkv_rope_append(hidden, w_qkv, cos, sin, position,
+                                                      cache_k, cache_v)
