@@ -92,13 +92,16 @@ def _close_rotated(got, want, pre):
     assert worst <= 1.0, f"error {worst:.3f} x the two-ulp bound"
 
 
+# Kernels and tiles the host picks on 148 SMs. One row tile (B * T <= 128), split-K clusters:
+# (2, 37, 2, 128) 16-feature tiles x 2 parts, (32, 1, 12, 768) 64 x 3, (2, 50, 3, 192) 16 x 3,
+# (3, 5, 2, 64) a single K slice (a cluster of one); the identity-rotation test below, 16 x 2. More rows, persistent: 128-feature tiles
+# for (1, 129, 4, 256), (3, 200, 12, 768), (4, 100, 6, 384), (4, 256, 12, 768); 64-feature
+# tiles for the odd head count of (5, 220, 5, 128).
 @pytest.mark.gpu
-# Feature-tile widths the host picks on 148 SMs: 16 for the first four, 64 for (3, 200, 12),
-# 32 for (4, 100, 6), 128 for (4, 256, 12); odd head counts need tiles of at most 64 features.
 @pytest.mark.parametrize("B,T,H,dim,position,cap", [
-    (2, 37, 2, 128, 5, 64), (32, 1, 12, 768, 100, 384), (1, 129, 4, 256, 3, 140),
-    (2, 50, 3, 192, 1, 64), (3, 200, 12, 768, 0, 256), (4, 100, 6, 384, 7, 128),
-    (4, 256, 12, 768, 0, 256), (5, 220, 5, 128, 0, 256)])
+    (2, 37, 2, 128, 5, 64), (32, 1, 12, 768, 100, 384), (2, 50, 3, 192, 1, 64),
+    (3, 5, 2, 64, 2, 16), (1, 129, 4, 256, 3, 140), (3, 200, 12, 768, 0, 256),
+    (4, 100, 6, 384, 7, 128), (4, 256, 12, 768, 0, 256), (5, 220, 5, 128, 0, 256)])
 @torch.no_grad()
 def test_qkv_rope_matches_unfused(B, T, H, dim, position, cap):
     _gpu()

@@ -64,35 +64,6 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8]) {
   f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
 }
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address of this CTA's shared-memory location `addr` in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b)
-               : "memory");
-}
-
-// Every thread of every CTA of the cluster: release this CTA's earlier shared-memory writes
-// (local and remote), then wait until all CTAs have arrived (acquire).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 __global__ void __launch_bounds__(THREADS, 4)
 decode_direct_kernel(const Params p) {
   __shared__ __align__(16) float qs[HD];

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "tt_attention.h"
@@ -256,33 +257,161 @@ bool encode_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t col
   return true;
 }
 
-template <int BN>
-cudaError_t set_qkv_rope_attribute() {
-  return cudaFuncSetAttribute(tt::qkv_rope::qkv_rope_append_kernel<BN>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(tt::qkv_rope::smem_bytes<BN>()));
+
+// Launch plan of the fused QKV kernel.
+// One row tile (B * T <= 128): split-K clusters. Per feature-tile width (64, 32, 16, widest
+// first) the largest K split S <= 3 (at most one part per K slice) whose clusters are all
+// resident at once (cudaOccupancyMaxActiveClusters: clusters of S CTAs fit per GPC, so S = 4
+// with 36 tiles already needs a second wave on 148 SMs); the first width whose grid covers 70 %
+// of the SMs is taken, else the widest grid. The partial sums of all parts meet in rank 0's
+// shared memory, and that reduction grows with S: on the decode shapes (B = 1..32, H = 12,
+// 768 features) 64-feature tiles x 3 parts measured fastest (4.7-5.2 us against 5.1-13.9 for
+// 2, 4, 6 or 8 parts and for 32- or 16-feature tiles).
+// More rows: the persistent kernel over 128-feature tiles (64 with an odd head count, so that a
+// tile stays inside one of q, k, v), one CTA per SM.
+struct QkvRopePlan {
+  bool splitk = false;
+  int bn = 0;
+  int splits = 1;
+  int64_t n_tiles = 0, m_tiles = 0;
+  int red_rows = 0;
+  unsigned grid = 0;
+  size_t smem = 0;
+};
+
+size_t qkv_splitk_fixed(int bn) {
+  namespace qr = tt::qkv_rope;
+  return bn == 64 ? qr::splitk_fixed_bytes<64>()
+                  : bn == 32 ? qr::splitk_fixed_bytes<32>() : qr::splitk_fixed_bytes<16>();
 }
 
-// Feature-tile width of the fused QKV kernel: the widest of 128, 64, 32, 16 whose grid covers
-// at least 85 % of the SMs (one CTA per SM fits), else 16. 128-feature tiles span two heads, so
-// they need an even head count to stay inside one of q, k, v.
-int qkv_rope_tile_width(int64_t rows, int64_t heads, int sms) {
-  const int64_t m_tiles = (rows + tt::qkv_rope::BM - 1) / tt::qkv_rope::BM;
-  const int64_t n = 3 * heads * TT_ATTN_HEAD_DIM;
-  const int64_t want = (static_cast<int64_t>(sms > 0 ? sms : 148) * 85 + 99) / 100;
-  for (int bn : {128, 64, 32}) {
-    if (bn == 128 && heads % 2 != 0) continue;
-    if (m_tiles * (n / bn) >= want) return bn;
+constexpr size_t kMaxDynamicSmem = 227 * 1024;
+constexpr int kQkvMaxSplits = 3;
+
+// Clusters of `splits` split-K CTAs (feature tile bn, `smem` bytes each) resident at once on
+// the current device; cached, since every decode step asks.
+int qkv_max_clusters(int dev, int bn, int splits, size_t smem) {
+  namespace qr = tt::qkv_rope;
+  struct Key { int dev, bn, splits; size_t smem; int n; };
+  static std::mutex mu;
+  static std::vector<Key> cache;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Key& k : cache)
+      if (k.dev == dev && k.bn == bn && k.splits == splits && k.smem == smem) return k.n;
   }
-  return 16;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(splits), 1, 1);
+  cfg.blockDim = dim3(qr::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e;
+  if (bn == 64) e = cudaOccupancyMaxActiveClusters(&n, qr::qkv_rope_splitk_kernel<64>, &cfg);
+  else if (bn == 32) e = cudaOccupancyMaxActiveClusters(&n, qr::qkv_rope_splitk_kernel<32>, &cfg);
+  else e = cudaOccupancyMaxActiveClusters(&n, qr::qkv_rope_splitk_kernel<16>, &cfg);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;  // unknown: treated as "does not fit", so only S = 1 is taken
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() < 256) cache.push_back({dev, bn, splits, smem, n});
+  return n;
 }
 
-template <int BN>
-void launch_qkv_rope(const CUtensorMap& tm_h, const CUtensorMap& tm_w, const tt::qkv_rope::Params& p,
-                     int64_t n, int64_t m_tiles, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>(n / BN), static_cast<unsigned>(m_tiles));
-  tt::qkv_rope::qkv_rope_append_kernel<BN>
-      <<<grid, tt::qkv_rope::THREADS, tt::qkv_rope::smem_bytes<BN>(), stream>>>(tm_h, tm_w, p);
+QkvRopePlan qkv_rope_plan(int64_t rows, int64_t heads, int64_t dim, int dev, int sms) {
+  namespace qr = tt::qkv_rope;
+  QkvRopePlan pl;
+  const int64_t n = 3 * heads * TT_ATTN_HEAD_DIM;
+  const int64_t n_k = dim / qr::BK;
+  const int64_t sm = sms > 0 ? sms : 148;
+  pl.m_tiles = (rows + qr::BM - 1) / qr::BM;
+  if (pl.m_tiles == 1) {
+    pl.splitk = true;
+    pl.red_rows = static_cast<int>((rows + 7) / 8 * 8);
+    const int64_t want = (sm * 70 + 99) / 100;
+    QkvRopePlan best = pl;
+    for (int bn : {64, 32, 16}) {
+      const int64_t tiles = n / bn;
+      auto bytes = [&](int64_t k) {  // fixed part + k partial-sum buffers [rows][bn + 4]
+        return qkv_splitk_fixed(bn) + static_cast<size_t>(k) * (bn + 4) * pl.red_rows * 4;
+      };
+      int64_t sp = 1;
+      for (int64_t k = 2; k <= std::min<int64_t>(kQkvMaxSplits, n_k); ++k)
+        if (bytes(k) <= kMaxDynamicSmem &&
+            tiles <= qkv_max_clusters(dev, bn, static_cast<int>(k), bytes(k)))
+          sp = k;
+      QkvRopePlan c = pl;
+      c.bn = bn;
+      c.splits = static_cast<int>(sp);
+      c.n_tiles = tiles;
+      c.grid = static_cast<unsigned>(tiles * sp);
+      c.smem = bytes(sp);
+      if (best.bn == 0 || c.grid > best.grid) best = c;
+      if (tiles * sp >= want) return c;
+    }
+    return best;
+  }
+  pl.bn = heads % 2 == 0 ? 128 : 64;
+  pl.n_tiles = n / pl.bn;
+  pl.grid = static_cast<unsigned>(std::min<int64_t>(pl.m_tiles * pl.n_tiles, sm));
+  pl.smem = pl.bn == 128 ? qr::persistent_smem_bytes<128>() : qr::persistent_smem_bytes<64>();
+  return pl;
+}
+
+cudaError_t launch_qkv_rope(const QkvRopePlan& pl, const CUtensorMap& tm_h, const CUtensorMap& tm_w,
+                            const tt::qkv_rope::Params& p, cudaStream_t stream) {
+  namespace qr = tt::qkv_rope;
+  if (!pl.splitk) {
+    if (pl.bn == 128)
+      qr::qkv_rope_persistent_kernel<128><<<pl.grid, qr::THREADS, pl.smem, stream>>>(tm_h, tm_w, p);
+    else
+      qr::qkv_rope_persistent_kernel<64><<<pl.grid, qr::THREADS, pl.smem, stream>>>(tm_h, tm_w, p);
+    return cudaSuccess;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.splits), static_cast<unsigned>(pl.n_tiles), 1);
+  cfg.blockDim = dim3(qr::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(pl.splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (pl.bn == 64) return cudaLaunchKernelEx(&cfg, qr::qkv_rope_splitk_kernel<64>, tm_h, tm_w, p);
+  if (pl.bn == 32) return cudaLaunchKernelEx(&cfg, qr::qkv_rope_splitk_kernel<32>, tm_h, tm_w, p);
+  return cudaLaunchKernelEx(&cfg, qr::qkv_rope_splitk_kernel<16>, tm_h, tm_w, p);
+}
+
+cudaError_t set_qkv_rope_attributes() {
+  namespace qr = tt::qkv_rope;
+  const int split_max = static_cast<int>(kMaxDynamicSmem);
+  cudaError_t e = cudaFuncSetAttribute(qr::qkv_rope_persistent_kernel<128>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(qr::persistent_smem_bytes<128>()));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(qr::qkv_rope_persistent_kernel<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(qr::persistent_smem_bytes<64>()));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(qr::qkv_rope_splitk_kernel<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, split_max);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(qr::qkv_rope_splitk_kernel<32>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, split_max);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(qr::qkv_rope_splitk_kernel<16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, split_max);
+  return e;
 }
 
 // ------------------------------------------------------------------ per-device setup
@@ -360,10 +489,7 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
                                prefill_smem);
       if (e != cudaSuccess) break;
     }
-    if (e == cudaSuccess) e = set_qkv_rope_attribute<128>();
-    if (e == cudaSuccess) e = set_qkv_rope_attribute<64>();
-    if (e == cudaSuccess) e = set_qkv_rope_attribute<32>();
-    if (e == cudaSuccess) e = set_qkv_rope_attribute<16>();
+    if (e == cudaSuccess) e = set_qkv_rope_attributes();
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -556,14 +682,14 @@ TT_ATTN_API tt_attn_status tt_qkv_rope_append_bf16(
   int dev = 0, sm_count = 0;
   tt_attn_status st = prepare_device(&dev, &sm_count);
   if (st != TT_ATTN_OK) return st;
-  const int bn = qkv_rope_tile_width(rows, heads, sm_count);
+  const QkvRopePlan pl = qkv_rope_plan(rows, heads, dim, dev, sm_count);
   // One row tile: the h box covers only the rows that exist (TMA fills past M with zeros).
-  const uint32_t box_rows = m_tiles == 1 ? static_cast<uint32_t>((rows + 7) / 8 * 8)
-                                         : static_cast<uint32_t>(qr::BM);
+  const uint32_t box_rows = pl.splitk ? static_cast<uint32_t>(pl.red_rows)
+                                      : static_cast<uint32_t>(qr::BM);
   CUtensorMap tm_h, tm_w;
   std::string err;
   if (!encode_map_2d(&tm_h, hidden, rows, dim, box_rows, &err) ||
-      !encode_map_2d(&tm_w, w_qkv, n, dim, static_cast<uint32_t>(bn), &err))
+      !encode_map_2d(&tm_w, w_qkv, n, dim, static_cast<uint32_t>(pl.bn), &err))
     return fail(TT_ATTN_UNSUPPORTED, err);
   qr::Params p{};
   p.M = static_cast<int>(rows);
@@ -581,15 +707,14 @@ TT_ATTN_API tt_attn_status tt_qkv_rope_append_bf16(
   p.ck_s0 = ck_strides[0]; p.ck_s1 = ck_strides[1]; p.ck_s2 = ck_strides[2];
   p.cv_s0 = cv_strides[0]; p.cv_s1 = cv_strides[1]; p.cv_s2 = cv_strides[2];
   p.capacity = capacity;
-  p.stage_tx_bytes = (box_rows + static_cast<uint32_t>(bn)) * qr::BK * 2;
-  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  switch (bn) {
-    case 128: launch_qkv_rope<128>(tm_h, tm_w, p, n, m_tiles, cs); break;
-    case 64: launch_qkv_rope<64>(tm_h, tm_w, p, n, m_tiles, cs); break;
-    case 32: launch_qkv_rope<32>(tm_h, tm_w, p, n, m_tiles, cs); break;
-    default: launch_qkv_rope<16>(tm_h, tm_w, p, n, m_tiles, cs); break;
-  }
-  return check_launch("qkv_rope_append_kernel launch");
+  p.stage_tx_bytes = (box_rows + static_cast<uint32_t>(pl.bn)) * qr::BK * 2;
+  p.n_tiles = static_cast<int>(pl.n_tiles);
+  p.m_tiles = static_cast<int>(pl.m_tiles);
+  p.red_rows = pl.red_rows;
+  const cudaError_t le = launch_qkv_rope(pl, tm_h, tm_w, p, static_cast<cudaStream_t>(stream));
+  if (le != cudaSuccess)
+    return fail(TT_ATTN_LAUNCH_FAIL, std::string("qkv_rope_append launch: ") + cudaGetErrorString(le));
+  return check_launch("qkv_rope_append launch");
 }
 
 // Backward workspace: -LSE * log2(e) and -D per query row, each [B, H, Tq_pad] FP32 with Tq
