@@ -43,6 +43,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Add to the transaction count of the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
                ::"r"(smem_u32(bar)), "r"(bytes) : "memory");

@@ -82,6 +82,8 @@ int decode_chunk(int64_t bh, int64_t tk) {
 constexpr int64_t kDirectDecodeMaxKeys = 4096;
 constexpr int64_t kDirectDecodeMaxRows = int64_t(1) << 20;  // (batch * heads * kv_len): 256 MB of K/V
 
+constexpr int64_t kDirectDecodeMaxSplits = 4;
+
 bool use_direct_decode(int64_t bh, int64_t kv_len) {
   return kv_len <= kDirectDecodeMaxKeys && bh * kv_len <= kDirectDecodeMaxRows;
 }
@@ -490,6 +492,10 @@ tt_attn_status prepare_device(int* dev_out, int* sm_count = nullptr) {
       if (e != cudaSuccess) break;
     }
     if (e == cudaSuccess) e = set_qkv_rope_attributes();
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tt::decode_direct::decode_direct_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tt::decode_direct::kSmemBytes));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tt::decode::decode_split_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1029,16 +1035,29 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     p.H = static_cast<int>(heads);
     p.Tk = static_cast<int>(kv_len);
     const int64_t passes_total = (kv_len + dd::KEYS_PER_PASS - 1) / dd::KEYS_PER_PASS;
-    p.splits = static_cast<int>(std::min<int64_t>(dd::MAX_SPLITS, passes_total));
+    // CTAs per sequence: enough to fill three CTAs per SM, at most 4 (and one per chunk).
+    // Measured on B200 (graph replay, H = 12): B * H = 12 / 96 best at 4, 192 at 2, 384 and
+    // 768 at 1 (e.g. B = 32, Tk = 1024: 24.3 us at 1 against 39.5 at 8; B = 8, Tk = 4096:
+    // 23.9 at 4 against 30.3 at 8): with a two-stage ring per CTA, fewer and longer CTAs
+    // stream their chunks back to back, while each extra CTA pays the launch, the first load's
+    // latency and the cluster merge.
+    p.splits = static_cast<int>(std::max<int64_t>(
+        1, std::min<int64_t>({kDirectDecodeMaxSplits, passes_total,
+                              (3 * static_cast<int64_t>(sm_count > 0 ? sm_count : 148)) / bh})));
     p.keys_per_cta =
         static_cast<int>((passes_total + p.splits - 1) / p.splits) * dd::KEYS_PER_PASS;
     p.o = static_cast<__nv_bfloat16*>(out);
     p.lse = lse;
     p.scale_log2 = kScaleLog2;
+    CUtensorMap tmk, tmv;
+    std::string err;
+    if (!encode_map(&tmk, k, ks, &err, dd::KEYS_PER_PASS) ||
+        !encode_map(&tmv, v, vs, &err, dd::KEYS_PER_PASS))
+      return fail(TT_ATTN_UNSUPPORTED, err);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(bh * p.splits), 1, 1);
     cfg.blockDim = dim3(dd::THREADS, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = dd::kSmemBytes;
     cfg.stream = cs;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1047,7 +1066,7 @@ TT_ATTN_API tt_attn_status tt_attn_forward_bf16(
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t le = cudaLaunchKernelEx(&cfg, dd::decode_direct_kernel, p);
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, dd::decode_direct_kernel, tmk, tmv, p);
     if (le != cudaSuccess)
       return fail(TT_ATTN_LAUNCH_FAIL,
                   std::string("decode_direct_kernel launch: ") + cudaGetErrorString(le));
