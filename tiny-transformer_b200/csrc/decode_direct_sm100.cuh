@@ -189,16 +189,28 @@ decode_direct_kernel(const __grid_constant__ CUtensorMap tm_k,
       l = l * f + pr;
       float b0[4] = {a0 * f, 0.f, 0.f, 0.f}, b1[4] = {a1 * f, 0.f, 0.f, 0.f};
       // Features 2 lane, 2 lane + 1 of V row rr: byte 4 lane of the row, in piece lane / 4.
+      // Per half of the rows, all shared loads first, then all broadcasts of p, then the
+      // products: interleaved, each row's load waited for the previous row's shuffle and the
+      // loop ran as one latency chain (~1.7 us per chunk).
       const uint32_t vcol = static_cast<uint32_t>(lane & 3) << 2;
       const uint32_t vpiece = static_cast<uint32_t>(lane >> 2);
 #pragma unroll
-      for (int rr = 0; rr < 32; ++rr) {
-        if (rr < n_valid) {
-          const float pb = __shfl_sync(0xffffffffu, pr, rr);
-          const uint32_t vv = lds_u32(vbase + rr * ROW_BYTES +
-                                      ((vpiece ^ static_cast<uint32_t>(rr & 7)) << 4) + vcol);
-          b0[rr & 3] = fmaf(pb, bf16_lo(vv), b0[rr & 3]);
-          b1[rr & 3] = fmaf(pb, bf16_hi(vv), b1[rr & 3]);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t vv[16];
+        float pb[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int rr = half * 16 + i;
+          vv[i] = rr < n_valid ? lds_u32(vbase + rr * ROW_BYTES +
+                                         ((vpiece ^ static_cast<uint32_t>(rr & 7)) << 4) + vcol)
+                               : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pb[i] = __shfl_sync(0xffffffffu, pr, half * 16 + i);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          b0[i & 3] = fmaf(pb[i], bf16_lo(vv[i]), b0[i & 3]);
+          b1[i & 3] = fmaf(pb[i], bf16_hi(vv[i]), b1[i & 3]);
         }
       }
       a0 = (b0[0] + b0[1]) + (b0[2] + b0[3]);
