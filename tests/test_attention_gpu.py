@@ -266,10 +266,10 @@ def test_unaligned_and_strided_views(ext):
 
 
 def test_decode_split_boundaries_and_rescaling(ext):
-    # reference :289-310. Caches of up to 4096 keys take the cluster kernel: boundaries of its
-    # 32-row warp slices, 128-key passes and 1..8 CTAs per sequence (two passes per CTA past
-    # 1024 keys, four past 3072). Longer ones take the persistent split-KV kernel: 384-key ring
-    # stages, 384-key work items (six heads always take the smallest item) and long caches.
+    # reference :289-310. Six (batch, head) rows take the cluster kernel at every length here:
+    # boundaries of its 32-row warp slices, 128-key chunks, the two-stage ring (up to 17 chunks
+    # per CTA at 8193 keys) and 1..4 CTAs per sequence. The persistent split-KV kernel (over 2^20
+    # rows) is covered by the work-item, kv_lens and config-4 tests.
     for tk in (1, 2, 7, 31, 32, 33, 63, 64, 65, 127, 128, 129, 255, 256, 257, 383, 384, 385,
                511, 512, 513, 767, 768, 769, 1023, 1024, 1025, 1151, 1152, 1153, 1535, 1536,
                1537, 3072, 3073, 4095, 4096, 4097, 8192, 8193):
@@ -438,7 +438,7 @@ def test_rejects_sequence_index_overflow_before_copy(ext):
 @pytest.mark.parametrize("B,tk,chunk", [(90, 1025, 768), (90, 1536, 768), (100, 1537, 1536),
                                         (50, 3073, 1536), (50, 4608, 1536), (30, 4097, 768)])
 def test_decode_work_item_sizes(ext, B, tk, chunk):
-    """Caches large enough (over 2^20 (batch * head * key) rows, or over 4096 keys) for the
+    """Caches large enough (over 2^20 (batch * head * key) rows) for the
     persistent split-KV kernel, and enough heads that the host picks 768- and 1536-key work
     items: sequence ends on and beside item boundaries, with and without kv_lens. The chosen
     item size is read back from the workspace the C ABI asks for (a work counter, one arrival

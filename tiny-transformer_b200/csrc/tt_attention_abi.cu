@@ -76,16 +76,18 @@ int decode_chunk(int64_t bh, int64_t tk) {
 }
 
 // Decode path choice (shape only, so the workspace size never depends on the device): the
-// cluster kernel (decode_direct_sm100.cuh: no workspace, one launch, <= 8 CTAs per sequence)
-// unless the cache is long and the whole K/V read large, where the persistent split-KV kernel
-// (decode_sm100.cuh) streams closer to the HBM bandwidth.
-constexpr int64_t kDirectDecodeMaxKeys = 4096;
-constexpr int64_t kDirectDecodeMaxRows = int64_t(1) << 20;  // (batch * heads * kv_len): 256 MB of K/V
+// cluster kernel (decode_direct_sm100.cuh: no workspace, one launch, <= 4 CTAs per sequence)
+// up to 2^20 (batch * heads * kv_len) K/V rows (256 MB), the persistent split-KV kernel
+// (decode_sm100.cuh: dynamic work items balance uneven kv_lens) above. Measured with the L2
+// flushed: 201 MB (B = 16, H = 12, 4096 keys) 49 us against 72; 403 MB 78-82 us either way;
+// 805 MB with kv_lens 98 us against 92. Few long sequences (B = 8, H = 12, 8192 keys, 201 MB)
+// ran at 2.5 TB/s in the persistent kernel, so there is no separate key-count limit.
+constexpr int64_t kDirectDecodeMaxRows = int64_t(1) << 20;
 
 constexpr int64_t kDirectDecodeMaxSplits = 4;
 
 bool use_direct_decode(int64_t bh, int64_t kv_len) {
-  return kv_len <= kDirectDecodeMaxKeys && bh * kv_len <= kDirectDecodeMaxRows;
+  return bh * kv_len <= kDirectDecodeMaxRows;
 }
 
 // Prefill work plan (shape only, so the workspace size never depends on the device). A CTA
