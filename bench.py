@@ -851,6 +851,25 @@ def run_profile_case(which):
             dout = torch.randn_like(out)
             for _ in range(3):
                 ext.attention_backward(q, k, v, dout, out, lse, 0)
+        elif which == "cfg2":
+            q, k, v, _ = make_decode(torch, dict(CFG2, data_seed=CFG2["seed"]), with_lens=False)
+            for _ in range(3):
+                ext.attention_forward(q, k, v, CFG2["Tk"] - 1)
+        elif which == "qkv":
+            # The fused QKV projection + RoPE + cache append of one config-5 decode step
+            # (batch 32, 12 heads, width 768): the split-K cluster kernel.
+            from tiny_transformer_b200.operators import fused
+            g = torch.Generator(device="cuda").manual_seed(4200)
+            B, H, dim, cap = 32, 12, 768, 384
+            hidden = torch.randn(B, 1, dim, device="cuda", generator=g).bfloat16()
+            w = (torch.randn(3 * H * 64, dim, device="cuda", generator=g) * 0.05).bfloat16()
+            freq = 1.0 / 10000.0 ** (torch.arange(0, 64, 2, device="cuda").float() / 64)
+            ang = torch.arange(cap, device="cuda").float()[:, None] * freq
+            cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+            ck = torch.zeros(B, H, cap, 64, device="cuda", dtype=torch.bfloat16)
+            cv = torch.zeros_like(ck)
+            for _ in range(3):
+                fused.qkv_rope_append(hidden, w, cos, sin, 200, ck, cv)
         else:
             q, k, v, lens = make_decode(torch)
             for _ in range(3):
@@ -872,7 +891,8 @@ def main():
                     help="reference arm: largest CPU time one step may take")
     ap.add_argument("--no-generation", action="store_true",
                     help="leave the config-5 generation block out of the default line")
-    ap.add_argument("--profile", choices=("prefill", "decode", "backward"), default=None,
+    ap.add_argument("--profile", choices=("prefill", "decode", "backward", "cfg2", "qkv"),
+                    default=None,
                     help="run 3 launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
