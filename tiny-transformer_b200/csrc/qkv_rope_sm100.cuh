@@ -120,18 +120,26 @@ __device__ __forceinline__ bool wait_or_abort(volatile int& abort, uint64_t* bar
   }
 }
 
-__device__ __forceinline__ float bf16_round(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
+// Packed bf16 arithmetic (round to nearest even, one rounding per operation).
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
+__device__ __forceinline__ uint32_t bfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+constexpr uint32_t kMinusPlusOne = 0x3F80BF80u;  // bf16x2 (lo -1.0, hi +1.0)
 
-// (e, o) -> (e*c - o*s, e*s + o*c) with bf16 rounding after every operation (rope_append's
-// rotate_pair).
-__device__ __forceinline__ uint32_t rotate_pair(uint32_t pair, float c, float s) {
-  const float e = bf16_lo(pair);
-  const float o = bf16_hi(pair);
-  const float r0 = bf16_round(e * c) - bf16_round(o * s);
-  const float r1 = bf16_round(e * s) + bf16_round(o * c);
-  return pack_bf16x2(r0, r1);
+// (e, o) -> (e*c - o*s, o*c + e*s) on a bf16x2 pair, with the bf16 steps of rope_append (each
+// product rounded to bf16, then the difference / sum rounded): (e*c, o*c) and (o*s, e*s) by two
+// packed multiplies, then one packed FMA with (-1, +1) forms both results with one rounding
+// each. cc = (c, c) and ss = (s, s) hold the bf16-rounded cos / sin.
+__device__ __forceinline__ uint32_t rotate_pair2(uint32_t eo, uint32_t cc, uint32_t ss) {
+  const uint32_t oe = __byte_perm(eo, 0, 0x1032);
+  return bfma2(bmul2(oe, ss), kMinusPlusOne, bmul2(eo, cc));
 }
 
 // Where token row m goes: its batch / step and cache position; ok is false for rows past M and
@@ -156,34 +164,35 @@ __device__ __forceinline__ RowDest row_dest(const Params& p, int m) {
   return d;
 }
 
-// The bf16-rounded cos / sin of rotation pairs [i0, i0 + N) of position pos (N % 4 == 0).
+// cos / sin of rotation pairs [i0, i0 + N) of position pos (N % 4 == 0), rounded to bf16 and
+// duplicated into both halves of a bf16x2 word.
 template <int N>
-__device__ __forceinline__ void load_rotation(const Params& p, long long pos, int i0, float (&c)[N],
-                                              float (&sn)[N]) {
+__device__ __forceinline__ void load_rotation(const Params& p, long long pos, int i0,
+                                              uint32_t (&cc)[N], uint32_t (&ss)[N]) {
   const float4* c4 = reinterpret_cast<const float4*>(p.cos + pos * (HD / 2) + i0);
   const float4* s4 = reinterpret_cast<const float4*>(p.sin + pos * (HD / 2) + i0);
 #pragma unroll
   for (int g = 0; g < N / 4; ++g) {
     const float4 cv = __ldg(c4 + g), sv = __ldg(s4 + g);
-    c[4 * g] = bf16_round(cv.x); c[4 * g + 1] = bf16_round(cv.y);
-    c[4 * g + 2] = bf16_round(cv.z); c[4 * g + 3] = bf16_round(cv.w);
-    sn[4 * g] = bf16_round(sv.x); sn[4 * g + 1] = bf16_round(sv.y);
-    sn[4 * g + 2] = bf16_round(sv.z); sn[4 * g + 3] = bf16_round(sv.w);
+    cc[4 * g] = pack_bf16x2(cv.x, cv.x); cc[4 * g + 1] = pack_bf16x2(cv.y, cv.y);
+    cc[4 * g + 2] = pack_bf16x2(cv.z, cv.z); cc[4 * g + 3] = pack_bf16x2(cv.w, cv.w);
+    ss[4 * g] = pack_bf16x2(sv.x, sv.x); ss[4 * g + 1] = pack_bf16x2(sv.y, sv.y);
+    ss[4 * g + 2] = pack_bf16x2(sv.z, sv.z); ss[4 * g + 3] = pack_bf16x2(sv.w, sv.w);
   }
 }
 
 // Store SEG features [col, col + SEG) (col within the part, SEG | 64) of one token row: round to
-// bf16, rotate with the preloaded pairs c / sn (pair i of the segment) when `rotate`.
+// bf16, and for q and k rotate with the preloaded pairs cc / ss (pair i of the segment).
 template <int SEG>
 __device__ __forceinline__ void store_rotated(const Params& p, const RowDest& d, int part, int col,
-                                              const float (&v)[SEG], const float* c,
-                                              const float* sn) {
+                                              const float (&v)[SEG], const uint32_t* cc,
+                                              const uint32_t* ss) {
   const int head = col / HD, within = col % HD;
   uint32_t row[SEG / 2];
 #pragma unroll
   for (int i = 0; i < SEG / 2; ++i) {
     row[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-    if (part < 2) row[i] = rotate_pair(row[i], c[i], sn[i]);
+    if (part < 2) row[i] = rotate_pair2(row[i], cc[i], ss[i]);
   }
   __nv_bfloat16* dst;
   if (part == 0)
@@ -307,7 +316,7 @@ qkv_rope_splitk_kernel(const __grid_constant__ CUtensorMap tm_h,
   const int part = n0 / part_cols;
   const int items = p.red_rows * (BN / 16);
   const int et = static_cast<int>(threadIdx.x) - EPI_WARP0 * 32;  // epilogue thread 0..127
-  float c0[8] = {}, s0[8] = {};
+  uint32_t c0[8] = {}, s0[8] = {};
   RowDest d0{0, 0, 0, false};
   if (rank == 0 && warp >= EPI_WARP0 && et < items) {
     d0 = row_dest(p, et % p.red_rows);
@@ -347,7 +356,7 @@ qkv_rope_splitk_kernel(const __grid_constant__ CUtensorMap tm_h,
     for (int it = et; it < items; it += 4 * 32) {
       const int row = it % p.red_rows, seg = it / p.red_rows;
       RowDest d = d0;
-      float c[8], sn[8];
+      uint32_t c[8], sn[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) { c[i] = c0[i]; sn[i] = s0[i]; }
       const int col = n0 - part * part_cols + seg * 16;
@@ -484,7 +493,7 @@ qkv_rope_persistent_kernel(const __grid_constant__ CUtensorMap tm_h,
       // The row's destination and its 32 rotation pairs (the same for every head), fetched
       // before the accumulator is ready.
       const RowDest d = row_dest(p, m0 + r);
-      float c[HD / 2], sn[HD / 2];
+      uint32_t c[HD / 2], sn[HD / 2];
       if (d.ok && part < 2) load_rotation<HD / 2>(p, d.pos, 0, c, sn);
       if (!__all_sync(0xffffffffu, wait_or_abort(s.abort, &s.acc_full[a], (local >> 1) & 1)))
         break;
