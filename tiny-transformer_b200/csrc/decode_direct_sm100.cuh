@@ -22,11 +22,14 @@
 // while p_r is broadcast by shuffle. (Per-lane global loads of the rows held a 128-key pass at
 // ~3.5 us on L2-resident caches; a lane-per-feature score layout needed a 31-shuffle butterfly
 // per 32 keys.) Warps keep an online softmax across chunks; the CTA merges its warps in shared
-// memory, every CTA writes its (m, l, acc) record into the cluster leader's shared memory
-// (st.shared::cluster), one cluster barrier (release / acquire) publishes them, and the leader
-// merges the records into O and LSE. All CTAs of a cluster are co-scheduled and every CTA
-// reaches the barrier exactly once (a timed-out wait skips the remaining chunks, after the
-// copies in flight have landed), so the barrier always completes. Two 32 KiB stages per CTA
+// memory. A sequence on one CTA writes O and LSE from there, with no cluster barrier (a
+// barrier.cluster costs ~0.7 us even for a cluster of one). Otherwise every CTA writes its
+// (m, l, acc) record into the cluster leader's shared memory (st.shared::cluster), one cluster
+// barrier (release / acquire) publishes them, and the leader merges the records into O and
+// LSE (per-CTA mbarrier arrivals on the leader measured ~1 us slower than the barrier). All CTAs
+// of a cluster are co-scheduled and every CTA reaches the barrier exactly once (a timed-out wait
+// skips the remaining chunks, after the copies in flight have landed), so the barrier always
+// completes. Two 32 KiB stages per CTA
 // leave room for three CTAs per SM; the host sizes the split so that the grid fills them.
 #pragma once
 
@@ -239,13 +242,12 @@ decode_direct_kernel(const __grid_constant__ CUtensorMap tm_k,
     s.rec[warp][HD + 1] = l;
   }
   __syncthreads();
-  // Warp 0 merges the CTA's warps (weights exp2(m_w - M), never averaged outputs) and writes
-  // the CTA's record into the leader's crec[rank].
+  // Warp 0 merges the CTA's warps (weights exp2(m_w - M), never averaged outputs): the output
+  // of a sequence on one CTA, else the CTA's record for the leader's crec[rank].
+  float M = -INFINITY, n0 = 0.f, n1 = 0.f, den = 0.f;
   if (warp == 0) {
-    float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s.rec[w][HD]);
-    float n0 = 0.f, n1 = 0.f, den = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < WARPS; ++w) {
@@ -258,28 +260,34 @@ decode_direct_kernel(const __grid_constant__ CUtensorMap tm_k,
         den = fmaf(wt, s.rec[w][HD + 1], den);
       }
     }
-    const uint32_t dst = map_to_rank(smem_u32(s.crec[rank]), 0);
-    st_cluster_f32x2(dst + lane * 8, n0, n1);
-    if (lane == 0) {
-      st_cluster_f32(dst + HD * 4, M);
-      st_cluster_f32(dst + (HD + 1) * 4, den);
+    if (p.splits > 1) {
+      const uint32_t dst = map_to_rank(smem_u32(s.crec[rank]), 0);
+      st_cluster_f32x2(dst + lane * 8, n0, n1);
+      if (lane == 0) {
+        st_cluster_f32(dst + HD * 4, M);
+        st_cluster_f32(dst + (HD + 1) * 4, den);
+      }
     }
   }
-  cluster_sync();
-  if (rank != 0 || warp != 0) return;
-  float M = -INFINITY;
-  for (int c = 0; c < p.splits; ++c) M = fmaxf(M, s.crec[c][HD]);
-  float n0 = 0.f, n1 = 0.f, den = 0.f;
-  if (M != -INFINITY) {
-    for (int c = 0; c < p.splits; ++c) {
-      const float mc = s.crec[c][HD];
-      if (mc == -INFINITY) continue;
-      const float wt = ex2_approx(mc - M);
-      const float2 a = reinterpret_cast<const float2*>(s.crec[c])[lane];
-      n0 = fmaf(wt, a.x, n0);
-      n1 = fmaf(wt, a.y, n1);
-      den = fmaf(wt, s.crec[c][HD + 1], den);
+  if (p.splits > 1) {
+    cluster_sync();
+    if (rank != 0 || warp != 0) return;
+    M = -INFINITY;
+    for (int c = 0; c < p.splits; ++c) M = fmaxf(M, s.crec[c][HD]);
+    n0 = n1 = den = 0.f;
+    if (M != -INFINITY) {
+      for (int c = 0; c < p.splits; ++c) {
+        const float mc = s.crec[c][HD];
+        if (mc == -INFINITY) continue;
+        const float wt = ex2_approx(mc - M);
+        const float2 a = reinterpret_cast<const float2*>(s.crec[c])[lane];
+        n0 = fmaf(wt, a.x, n0);
+        n1 = fmaf(wt, a.y, n1);
+        den = fmaf(wt, s.crec[c][HD + 1], den);
+      }
     }
+  } else if (warp != 0) {
+    return;
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   reinterpret_cast<uint32_t*>(p.o + static_cast<size_t>(bh) * HD)[lane] =
