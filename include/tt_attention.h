@@ -58,7 +58,8 @@ typedef enum tt_attn_status {
  *   lse      contiguous [batch, heads, q_len] fp32, natural log
  *   workspace / workspace_bytes: device scratch of at least
  *            tt_attn_forward_workspace_size(...) bytes (may be NULL when that is 0). Decode
- *            (q_len == 1) of more than 2^20 (batch * heads * kv_len) K/V rows keeps a work
+ *            (q_len == 1) of more than 2^20 (batch * heads * kv_len) K/V rows (2^21 when
+ *            batch * heads <= 640) keeps a work
  *            counter and per-sequence arrival counters there, which the call zeroes on
  *            `stream` before its kernel runs, and its split-KV partials; prefill with fewer
  *            256-row query blocks than SMs keeps the partial records of its split blocks.
@@ -227,7 +228,8 @@ TT_ATTN_API int tt_attn_abi_version(void);
  * of that device changed (cudaDeviceReset, or a context the caller made current); make those
  * calls before any stream capture. All calls share the array: calls whose kernels overlap on
  * the GPU (different streams, or different host threads) race on it and must be serialised
- * by the caller. Caches of up to 2^20 (batch * heads * kv_len) K/V rows use no scratch at all.
+ * by the caller. Caches of up to 2^20 (batch * heads * kv_len) K/V rows, or up to 2^21 in at
+ * most 640 (batch, head) sequences, use no scratch at all.
  */
 TT_ATTN_API tt_attn_status tt_attn_decode_bf16_noalloc(
     const void* q, const int64_t* q_strides,

@@ -436,9 +436,10 @@ def test_rejects_sequence_index_overflow_before_copy(ext):
 
 
 @pytest.mark.parametrize("B,tk,chunk", [(90, 1025, 768), (90, 1536, 768), (100, 1537, 1536),
-                                        (50, 3073, 1536), (50, 4608, 1536), (30, 4097, 768)])
+                                        (60, 3073, 1536), (50, 4608, 1536), (30, 6000, 1536)])
 def test_decode_work_item_sizes(ext, B, tk, chunk):
-    """Caches large enough (over 2^20 (batch * head * key) rows) for the
+    """Caches large enough (over 2^20 (batch * head * key) rows with more than 640 sequences, or
+    over 2^21 rows) for the
     persistent split-KV kernel, and enough heads that the host picks 768- and 1536-key work
     items: sequence ends on and beside item boundaries, with and without kv_lens. The chosen
     item size is read back from the workspace the C ABI asks for (a work counter, one arrival

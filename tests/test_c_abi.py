@@ -88,14 +88,17 @@ def test_workspace_and_layout_queries(lib):
     n = lib.tt_attn_forward_workspace_size(64, 12, 1, 4096)
     arrivals = -(-64 * 12 * 4 // 256) * 256       # one counter per (batch, head), 256-B rounded
     assert n > 256 + arrivals and (n - 256 - arrivals) % (68 * 4) == 0  # counters + partials
-    # Caches of at most 2^20 (batch * head * key) rows take the cluster kernel: no workspace.
+    # Caches of at most 2^20 (batch * head * key) rows, or of at most 2^21 rows in at most 640
+    # sequences, take the cluster kernel: no workspace.
     assert lib.tt_attn_forward_workspace_size(8, 12, 1, 16) == 0
     assert lib.tt_attn_forward_workspace_size(8, 12, 1, 4096) == 0
     assert lib.tt_attn_forward_workspace_size(8, 12, 1, 8192) == 0
-    assert lib.tt_attn_forward_workspace_size(256, 1, 1, 4096) == 0
-    assert lib.tt_attn_forward_workspace_size(1, 1, 1, 1 << 20) == 0
-    assert lib.tt_attn_forward_workspace_size(257, 1, 1, 4096) > 0
-    assert lib.tt_attn_forward_workspace_size(1, 1, 1, (1 << 20) + 1) > 0
+    assert lib.tt_attn_forward_workspace_size(16, 12, 1, 8192) == 0
+    assert lib.tt_attn_forward_workspace_size(1, 1, 1, 1 << 21) == 0
+    assert lib.tt_attn_forward_workspace_size(640, 1, 1, 2048) == 0
+    assert lib.tt_attn_forward_workspace_size(641, 1, 1, 2048) > 0
+    assert lib.tt_attn_forward_workspace_size(1, 1, 1, (1 << 21) + 1) > 0
+    assert lib.tt_attn_forward_workspace_size(32, 12, 1, 8192) > 0
     # Enough sequences that each takes one 1536-key item: the work counter only.
     assert lib.tt_attn_forward_workspace_size(100, 12, 1, 1500) == 256
     assert lib.tt_attn_forward_workspace_size(8, 12, 512, 512) == 0  # enough CTAs: no split

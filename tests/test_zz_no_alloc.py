@@ -80,9 +80,9 @@ def _no_alloc(lib, q, k, v, lens):
 
 @torch.no_grad()
 def test_no_alloc_decode_matches_workspace_entry_point_twice(lib):
-    # Two calls in a row, with caches large enough (over 2^20 batch * head * key rows) for the
-    # split-KV kernel that uses the scratch.
-    cases = [(11, 24, 12, 4000, False), (12, 40, 8, 3500, True)]
+    # Two calls in a row, with caches large enough (over 2^20 batch * head * key rows in more
+    # than 640 sequences) for the split-KV kernel that uses the scratch.
+    cases = [(11, 64, 12, 2048, False), (12, 56, 12, 2100, True)]
     for seed, B, H, Tk, with_lens in cases:
         q, k, v, lens = _inputs(seed, B, H, Tk, with_lens)
         ref_o, ref_lse = _with_workspace(lib, q, k, v, lens)

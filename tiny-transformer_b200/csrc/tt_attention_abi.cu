@@ -77,17 +77,24 @@ int decode_chunk(int64_t bh, int64_t tk) {
 
 // Decode path choice (shape only, so the workspace size never depends on the device): the
 // cluster kernel (decode_direct_sm100.cuh: no workspace, one launch, <= 4 CTAs per sequence)
-// up to 2^20 (batch * heads * kv_len) K/V rows (256 MB), the persistent split-KV kernel
-// (decode_sm100.cuh: dynamic work items balance uneven kv_lens) above. Measured with the L2
-// flushed: 201 MB (B = 16, H = 12, 4096 keys) 49 us against 72; 403 MB 78-82 us either way;
-// 805 MB with kv_lens 98 us against 92. Few long sequences (B = 8, H = 12, 8192 keys, 201 MB)
-// ran at 2.5 TB/s in the persistent kernel, so there is no separate key-count limit.
+// up to 2^20 (batch * heads * kv_len) K/V rows (256 MB), and up to 2^21 rows when there are at
+// most 640 (batch, head) sequences; the persistent split-KV kernel (decode_sm100.cuh: dynamic
+// work items balance uneven kv_lens) above. Measured with the L2 flushed, full lengths / kv_lens
+// U[Tk/8, Tk]: 1.57M rows as 192 sequences of 8192 keys 82.9 / 60.4 us against 96.3 / 69.5 in
+// the persistent kernel, 1.18M rows as 576 sequences 68.5 / 48.2 against 73.7 / 55.3, but 1.57M
+// rows as 768 or 1536 sequences 80-81 / 58 against 78-80 / 55-57; 3.1M rows (384 sequences,
+// kv_lens) 98 against 90. Few long sequences ran at 1.6-2.5 TB/s in the persistent kernel, so
+// there is no separate key-count limit.
 constexpr int64_t kDirectDecodeMaxRows = int64_t(1) << 20;
+constexpr int64_t kDirectDecodeFewSeqMaxRows = int64_t(1) << 21;
+constexpr int64_t kDirectDecodeFewSeq = 640;
 
 constexpr int64_t kDirectDecodeMaxSplits = 4;
 
 bool use_direct_decode(int64_t bh, int64_t kv_len) {
-  return bh * kv_len <= kDirectDecodeMaxRows;
+  const int64_t rows = bh * kv_len;
+  return rows <= kDirectDecodeMaxRows ||
+         (bh <= kDirectDecodeFewSeq && rows <= kDirectDecodeFewSeqMaxRows);
 }
 
 // Prefill work plan (shape only, so the workspace size never depends on the device). A CTA
