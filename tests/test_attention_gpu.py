@@ -459,6 +459,22 @@ def test_decode_work_item_sizes(ext, B, tk, chunk):
     check_forward(ext, q, k, v, tk - 1, kv_lens=lens.cuda())
 
 
+@pytest.mark.parametrize("B,H,tk", [(24, 12, 384), (32, 12, 513), (20, 12, 1100)])
+def test_decode_one_cta_per_sequence(ext, B, H, tk):
+    """Enough (batch, head) sequences (B * H >= 223) that the cluster decode kernel gives each
+    sequence a single CTA, which writes O and LSE from its own merge without a cluster barrier:
+    whole caches, 128-key chunk and ring boundaries through kv_lens, and empty sequences."""
+    from tiny_transformer_b200.operators._extension import load_c_abi
+    assert load_c_abi().tt_attn_forward_workspace_size(B, H, 1, tk) == 0  # the cluster kernel
+    torch.manual_seed(B * tk)
+    q = torch.randn(B, H, 1, 64, device="cuda", dtype=torch.bfloat16)
+    k, v = [torch.randn(B, H, tk, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    check_forward(ext, q, k, v, tk - 1)
+    edges = [1, 31, 32, 33, 127, 128, 129, 255, 256, 257, tk - 1, tk, 0]
+    lens = torch.tensor([min(edges[b % len(edges)], tk) for b in range(B)], dtype=torch.int32)
+    check_forward(ext, q, k, v, tk - 1, kv_lens=lens.cuda())
+
+
 # ----------------------------------------------------------------------------- kv_lens (new)
 def test_kv_lens_masks_beyond_length(ext):
     """Key j visible iff j < kv_lens[b]: NaN-poisoned cache beyond each length, lengths on chunk
