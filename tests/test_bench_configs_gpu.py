@@ -99,9 +99,11 @@ def test_cfg4_every_sequence(ext):
         mx, _ = _check(_np(out[b:b + 1]), _np(lse[b:b + 1]), _np(q[b:b + 1]),
                        _np(k[b:b + 1, :, :L]), _np(v[b:b + 1, :, :L]), L - 1)
         worst = max(worst, mx)
-    # The batch shards of the multi-GPU bench: a smaller batch may pick a smaller split-KV
-    # chunk, so the FP32 merge order (not the result's accuracy) can differ from the whole call.
-    for shard in (bench.decode_shard(8, r, lens_np) for r in range(8)):
+    # The batch shards of the multi-GPU bench at 2, 4 and 8 ranks (the split-KV kernel, then
+    # the cluster kernel): a smaller batch may take another kernel or split, so the FP32 merge
+    # order (not the result's accuracy) can differ from the whole call.
+    shards = [bench.decode_shard(w, r, lens_np) for w in (2, 4, 8) for r in range(w)]
+    for shard in shards:
         sl = slice(shard.start, shard.stop)
         o_s, l_s = ext.attention_forward(q[sl], k[sl], v[sl], c["Tk"] - 1, None, lens[sl])
         torch.testing.assert_close(o_s, out[sl], atol=1e-2, rtol=1e-2)
