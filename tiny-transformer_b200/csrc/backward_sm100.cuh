@@ -121,8 +121,8 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_
 // are the TMEM lanes). Per step, all products are M = 128 tcgen05 MMAs:
 //   S^T = K.Q^T, dP^T = V.dO^T        (SS, N = 128)
 //   dV += P^T.dO                      (TS, A = bf16 P^T in its own TMEM columns)
-//   dK += dS^T.Q                      (TS, A = bf16 dS^T written over dP^T)
-//   dQ_step = dS.K                    (SS, A = dS staged in shared memory, MN-major)
+//   dK += dS^T.Q                      (SS, A = the shared-memory dS tile read K-major)
+//   dQ_step = dS.K                    (SS, A = the same dS tile read MN-major)
 // dQ_step is read out of TMEM by four drain warps and added into an FP32 dQ workspace with TMA
 // bulk reduce-add (one 32 x 32 box per warp and feature half); bwd_dq_convert_kernel scales it
 // and rounds it to bf16 afterwards. S, dP and the exponentials are computed once per pair of
@@ -130,16 +130,16 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_
 //
 // The elementwise warps work in two phases per step: (1) load S^T, release it, compute
 // P = exp2(S * scale * log2(e) - LSE * log2(e)) and store bf16 P^T; (2) load dP^T, compute
-// dS = P * (dP - D) from the FP32 P kept in registers, store bf16 dS^T over dP^T and dS into
-// shared memory. Two issuer threads feed the tensor core (a tcgen05.mma blocks its thread for
+// dS = P * (dP - D) from the FP32 P kept in registers, store bf16 dS into shared memory.
+// Two issuer threads feed the tensor core (a tcgen05.mma blocks its thread for
 // about its execution time, so one thread would delay each product behind the others):
 //   scores issuer:     S^T(i+1) once S^T(i) is released (overlapping both phases of step i);
-//                      dP^T(i+1) once dK(i) has completed (it overwrites dS^T(i));
+//                      dP^T(i+1) once the elementwise warps have read dP^T(i);
 //   accumulate issuer: dV(i) once P^T(i) is stored; dK(i), then dQ(i), once dS(i) is stored;
 // so phase 1 of step i+1 starts as soon as phase 2 of step i ends. (Measured on cfg3 against
 // other assignments: S and dV on one thread with dK, dP, dQ on the other, 5 % slower; three
 // issuer warps, 2-5 % slower.)
-// TMEM: S^T [0,128), dP^T/dS^T [128,256), dV [256,320), dK [320,384), dQ [384,448),
+// TMEM: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448),
 // P^T [448,512) of 512 columns.
 // Roles: warps 0-7 elementwise (warp w: TMEM lanes 32 (w % 4) .., query columns 64 (w / 4) ..),
 // warps 8-11 dQ drain (lanes 32 (w % 4) ..), warp 12 TMA producer, warp 13 accumulate issuer
@@ -179,7 +179,7 @@ struct alignas(1024) Smem {
   float nd[STAGES][T];     // -D per query row of the stage
   uint64_t kv_full;
   uint64_t q_full[STAGES], q_empty[STAGES];
-  uint64_t s_full, s_consumed, p_full, pv_free, dp_full, ds_ready, ds_free, dk_done;
+  uint64_t s_full, s_consumed, p_full, pv_free, dp_full, ds_ready, ds_free;
   uint64_t dq_full, dq_free, acc_final, drain, drain_scores;
   uint32_t tmem_base;
   volatile int abort;
@@ -197,17 +197,27 @@ __device__ __forceinline__ void issue_dq(uint32_t tmem_d, uint32_t ds_addr, uint
             make_sdesc_sw128(k_addr + kk * 2048, 8192, 1024), idesc, kk > 0 ? 1u : 0u);
 }
 
-// D += A.B, K = 128 rows in 8 steps of 16, B = a 128 x 64 MN-major tile (2048 B per step).
-// A = bf16 pairs in TMEM: DENSE, 8 columns per step from tmem_a; otherwise chunk c of 32 K rows
-// at columns [32c, 32c + 16) (the layout written over a 128-column FP32 region).
-template <bool DENSE>
-__device__ __forceinline__ void issue_accumulate128(uint32_t tmem_d, uint32_t tmem_a,
-                                                    uint32_t b_addr, uint32_t idesc,
-                                                    bool accumulate) {
+// dV += P^T.dO: A = bf16 P^T pairs in TMEM (8 columns per k-step), B = dO (MN-major over
+// features), K = 128 queries in 8 steps of 16 rows (2048 B per step).
+__device__ __forceinline__ void issue_dv(uint32_t tmem_d, uint32_t tmem_a, uint32_t b_addr,
+                                         uint32_t idesc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < T / 16; ++kk)
-    umma_ts(tmem_d, tmem_a + (DENSE ? 8 * kk : 32 * (kk >> 1) + 8 * (kk & 1)),
-            make_sdesc_sw128(b_addr + kk * 2048, 8192, 1024), idesc,
+    umma_ts(tmem_d, tmem_a + 8 * kk, make_sdesc_sw128(b_addr + kk * 2048, 8192, 1024), idesc,
+            (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// dK += dS^T.Q: A = the shared-memory dS tile read as a K-major operand (row = key, 64 queries
+// of one atom column per 128-byte row, so k-step kk is 32 bytes into atom column kk / 4),
+// B = Q (MN-major over features, 2048 B per 16-query step). Reading dS from shared memory
+// leaves the dP^T columns free for the next step's dP^T as soon as the elementwise warps have
+// read them, instead of after dK.
+__device__ __forceinline__ void issue_dk(uint32_t tmem_d, uint32_t ds_addr, uint32_t q_addr,
+                                         uint32_t idesc, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < T / 16; ++kk)
+    umma_ss(tmem_d, make_sdesc_sw128(ds_addr + (kk >> 2) * (T * 128) + (kk & 3) * 32, 16, 1024),
+            make_sdesc_sw128(q_addr + kk * 2048, 8192, 1024), idesc,
             (accumulate || kk > 0) ? 1u : 0u);
 }
 
@@ -284,7 +294,6 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     mbar_init(&s.dp_full, 1);
     mbar_init(&s.ds_ready, EW_WARPS);
     mbar_init(&s.ds_free, 1);
-    mbar_init(&s.dk_done, 1);
     mbar_init(&s.dq_full, 1);
     mbar_init(&s.dq_free, 4);
     mbar_init(&s.acc_final, 1);
@@ -348,8 +357,8 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tc_fence_after();
         issue_scores(tmem + T_ST, k_addr, smem_u32(s.q[sn]), idesc_s);
         umma_commit(&s.s_full);
-        // dP^T(i+1) overwrites dS^T(i): after dK(i) has completed.
-        if (!wait_or_abort(s, &s.dk_done, i & 1)) break;
+        // dP^T(i+1) overwrites dP^T(i): once the elementwise warps have read it.
+        if (!wait_or_abort(s, &s.ds_ready, i & 1)) break;
         tc_fence_after();
         issue_scores(tmem + T_DPT, v_addr, smem_u32(s.dO[sn]), idesc_s);
         umma_commit(&s.dp_full);
@@ -366,12 +375,11 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const int st = i % STAGES;
         if (!wait_or_abort(s, &s.p_full, i & 1)) break;
         tc_fence_after();
-        issue_accumulate128<true>(tmem + T_DV, tmem + T_P, smem_u32(s.dO[st]), idesc_o, i > 0);
+        issue_dv(tmem + T_DV, tmem + T_P, smem_u32(s.dO[st]), idesc_o, i > 0);
         umma_commit(&s.pv_free);
         if (!wait_or_abort(s, &s.ds_ready, i & 1)) break;
         tc_fence_after();
-        issue_accumulate128<false>(tmem + T_DK, tmem + T_DPT, smem_u32(s.q[st]), idesc_o, i > 0);
-        umma_commit(&s.dk_done);
+        issue_dk(tmem + T_DK, smem_u32(s.ds[0]), smem_u32(s.q[st]), idesc_o, i > 0);
         // Q(i) and dO(i) were last read by dV(i) and dK(i); S^T(i) and dP^T(i) (scores
         // issuer) completed before the elementwise warps could read them.
         umma_commit(&s.q_empty[st]);
@@ -489,8 +497,6 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tmem_wait_ld();
         reg_fence16(dr);
         ew_dscores(pr + 16 * c, dr, nd_addr + 64 * c, dsb);
-        // over dP^T columns just read: 32-query chunk 2 * half + c / 2, 8 columns per 16 queries
-        tmem_st8(tmem + lane_base + T_DPT + 32 * (2 * half + (c >> 1)) + 8 * (c & 1), dsb);
         // The dS tile was last read by dQ(i - 1).
         if (c == 0 && i > 0 && !warp_wait(s, &s.ds_free, (i - 1) & 1)) {
           ok = false;
@@ -501,7 +507,6 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         sts_u4(ds_row + (((j + 1) ^ sw) << 4), dsb[4], dsb[5], dsb[6], dsb[7]);
       }
       if (!ok) break;
-      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
