@@ -9,9 +9,10 @@
 //   dQ_i  = scale * sum_j bf16(dS_ij) k_j                      (FP32 accumulate, BF16 out)
 // with key j visible to query i iff j <= i + past_len (Tk == Tq + past_len), scale = 1/8.
 //
-// Three kernels, in stream order (after a memset of the FP32 dQ accumulator):
+// Three kernels, in stream order:
 // * bwd_preprocess_kernel: -D and -LSE * log2(e) per query row, in rows padded to whole
-//   128-row tiles (eight lanes per row, 16-byte loads of dO and O).
+//   128-row tiles (eight lanes per row, 16-byte loads of dO and O), and zeros for the row's
+//   FP32 dQ accumulator (the same pass instead of a separate memset).
 // * fused::bwd_fused_kernel: one CTA per (b, h, 128-key tile); S, dP and the exponentials are
 //   computed once per (query tile, key tile) pair and feed dV, dK and dQ (see below).
 // * fused::bwd_dq_convert_kernel: dQ = bf16(scale * dQ accumulator).
@@ -40,6 +41,7 @@ struct PreParams {
   const float* lse;          // contiguous [B * H * Tq], natural log
   float* nlse2;              // [B * H * Tq_pad]: -LSE * log2(e), -inf on padding rows
   float* nd;                 // [B * H * Tq_pad]: -D, 0 on padding rows
+  float* dq_acc;             // [B * H * Tq, 64]: set to zero
 };
 
 // Eight lanes per row, 16-byte loads: a warp covers four rows, a block of 256 threads 32.
@@ -61,6 +63,9 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const PreParams p) 
           bf16_lo(a.y) * bf16_lo(o.y) + bf16_hi(a.y) * bf16_hi(o.y) +
           bf16_lo(a.z) * bf16_lo(o.z) + bf16_hi(a.z) * bf16_hi(o.z) +
           bf16_lo(a.w) * bf16_lo(o.w) + bf16_hi(a.w) * bf16_hi(o.w);
+    float4* acc = reinterpret_cast<float4*>(p.dq_acc + row * HD) + 2 * part;
+    acc[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   // Reduce over the eight lanes of the row (all 32 lanes take part in every shuffle).
 #pragma unroll
@@ -124,7 +129,8 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_
 //   dK += dS^T.Q                      (SS, A = the shared-memory dS tile read K-major)
 //   dQ_step = dS.K                    (SS, A = the same dS tile read MN-major)
 // dQ_step is read out of TMEM by four drain warps and added into an FP32 dQ workspace with TMA
-// bulk reduce-add (one 32 x 32 box per warp and feature half); bwd_dq_convert_kernel scales it
+// bulk reduce-add (32 x 32 boxes, the two feature halves of a warp's rows one after the other
+// through one staging box); bwd_dq_convert_kernel scales it
 // and rounds it to bf16 afterwards. S, dP and the exponentials are computed once per pair of
 // tiles, and every score product has N = 128.
 //
@@ -173,8 +179,8 @@ struct alignas(1024) Smem {
   // dS of the step as the MN-major A operand of dQ = dS.K: atom column c (queries [64c, 64c+64))
   // holds one 128-byte row per key (K index), 16-byte chunks XOR-swizzled by key & 7.
   uint8_t ds[2][T * 128];
-  // Per drain warp, the two feature halves of its 32 dQ rows, 128-byte swizzled.
-  uint8_t dq_stage[4][2][DQ_BOX_ROWS * 128];
+  // Per drain warp, one feature half of its 32 dQ rows at a time, 128-byte swizzled.
+  uint8_t dq_stage[4][DQ_BOX_ROWS * 128];
   float nlse2[STAGES][T];  // -LSE * log2(e) per query row of the stage (-inf past Tq)
   float nd[STAGES][T];     // -D per query row of the stage
   uint64_t kv_full;
@@ -398,8 +404,7 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     // dQ drain: thread = query row 32 * quarter + lane of the step = TMEM lane.
     const int quarter = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t* box0 = s.dq_stage[quarter][0];
-    uint8_t* box1 = s.dq_stage[quarter][1];
+    uint8_t* box = s.dq_stage[quarter];
     for (int i = 0; i < n_q; ++i) {
       if (!warp_wait(s, &s.dq_full, i & 1)) break;
       tc_fence_after();
@@ -417,19 +422,28 @@ bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       __syncwarp();
       const uint32_t sw = lane & 7;
-      const uint32_t row0_addr = smem_u32(box0) + lane * 128;
-      const uint32_t row1_addr = smem_u32(box1) + lane * 128;
+      const uint32_t row_addr = smem_u32(box) + lane * 128;
+      const int row0 = (qt0 + i) * T + quarter * DQ_BOX_ROWS;
+      // One staging box per warp: features [0, 32), then [32, 64) once the first reduce has
+      // read the box.
 #pragma unroll
-      for (uint32_t j = 0; j < 8; ++j) {
-        sts_u4(row0_addr + ((j ^ sw) << 4), a0[4 * j], a0[4 * j + 1], a0[4 * j + 2], a0[4 * j + 3]);
-        sts_u4(row1_addr + ((j ^ sw) << 4), a1[4 * j], a1[4 * j + 1], a1[4 * j + 2], a1[4 * j + 3]);
-      }
+      for (uint32_t j = 0; j < 8; ++j)
+        sts_u4(row_addr + ((j ^ sw) << 4), a0[4 * j], a0[4 * j + 1], a0[4 * j + 2], a0[4 * j + 3]);
       fence_proxy_async_smem();
       __syncwarp();
-      const int row0 = (qt0 + i) * T + quarter * DQ_BOX_ROWS;
       if (lane == 0 && row0 < p.Tq) {  // rows past Tq inside a box are clipped by the map
-        tma_reduce_add_4d(box0, &tm_dqacc, 0, row0, h, b);
-        tma_reduce_add_4d(box1, &tm_dqacc, 32, row0, h, b);
+        tma_reduce_add_4d(box, &tm_dqacc, 0, row0, h, b);
+        bulk_commit_group();
+        bulk_wait_group_read_all();
+      }
+      __syncwarp();
+#pragma unroll
+      for (uint32_t j = 0; j < 8; ++j)
+        sts_u4(row_addr + ((j ^ sw) << 4), a1[4 * j], a1[4 * j + 1], a1[4 * j + 2], a1[4 * j + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 < p.Tq) {
+        tma_reduce_add_4d(box, &tm_dqacc, 32, row0, h, b);
         bulk_commit_group();
       }
     }

@@ -875,7 +875,6 @@ tt_attn_status backward_impl(
   float* nlse2 = static_cast<float*>(workspace);
   float* nd = nlse2 + pad_rows;
   float* dq_acc = nd + pad_rows;
-  const size_t acc_bytes = static_cast<size_t>(rows) * TT_ATTN_HEAD_DIM * sizeof(float);
 
   constexpr unsigned tile = tt::backward::fused::T;
   CUtensorMap tmq, tmdo, tmk, tmv, tmacc;
@@ -884,10 +883,6 @@ tt_attn_status backward_impl(
       !encode_map(&tmk, k, ks, &err, tile) || !encode_map(&tmv, v, vs, &err, tile) ||
       !encode_map_f32(&tmacc, dq_acc, dos, &err, tt::backward::fused::DQ_BOX_ROWS))
     return fail(TT_ATTN_UNSUPPORTED, err);
-
-  cudaError_t e = cudaMemsetAsync(dq_acc, 0, acc_bytes, cs);
-  if (e != cudaSuccess)
-    return fail(TT_ATTN_LAUNCH_FAIL, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
 
   tt::backward::PreParams pp{};
   pp.rows = pad_rows;
@@ -898,6 +893,7 @@ tt_attn_status backward_impl(
   pp.lse = lse;
   pp.nlse2 = nlse2;
   pp.nd = nd;
+  pp.dq_acc = dq_acc;
   const int64_t pre_blocks =
       (pad_rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK;
   tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>(pre_blocks), 256, 0, cs>>>(pp);
