@@ -119,12 +119,12 @@ TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear);
  *   lse         contiguous [batch, heads, q_len] FP32, natural log (the forward's LSE)
  *   dq          contiguous [batch, heads, q_len, 64] bf16 output
  *   dk, dv      contiguous [batch, heads, kv_len, 64] bf16 outputs
- *   workspace   tt_attn_backward_workspace_size() bytes, 16-byte aligned (the FP32 row sums D
- *               and the FP32 dQ accumulator; its contents on entry do not matter)
+ *   workspace   tt_attn_backward_workspace_size() bytes, 16-byte aligned (the FP32 row sums D,
+ *               the FP32 dQ accumulator and a work counter; its contents on entry do not matter)
  *
  * Mask: key j visible to query i iff j <= i + past_len, kv_len == q_len + past_len.
- * On `stream`, in order: a memset of the dQ accumulator, then three kernels (row sums D; one
- * fused dQ/dK/dV kernel; dQ scaling to bf16). Nothing is allocated.
+ * On `stream`, in order, three kernels: row sums D (which also zeroes the dQ accumulator), one
+ * fused dQ/dK/dV kernel, dQ scaling to bf16. Nothing is allocated.
  */
 TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
     const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,

@@ -158,7 +158,7 @@ def test_backward_unsupported_layout_and_workspace_size(lib):
     assert lib.tt_attn_backward_bf16(16, qs, 16, ks, 16, ks, 16, 16, 16, 1, 1, 4, 4, 64, 0,
                                      16, 16, 16, 256, 1 << 20, None) == 2  # UNSUPPORTED
     # -LSE * log2(e) and -D for 6 heads x 128 padded rows, then the 30 x 64 FP32 dQ accumulator.
-    assert lib.tt_attn_backward_workspace_size(2, 3, 5) == 2 * 6 * 128 * 4 + 2 * 3 * 5 * 64 * 4
+    assert lib.tt_attn_backward_workspace_size(2, 3, 5) == 2 * 6 * 128 * 4 + 2 * 3 * 5 * 64 * 4 + 16
     assert lib.tt_attn_backward_workspace_size(0, 3, 5) == 0
 
 

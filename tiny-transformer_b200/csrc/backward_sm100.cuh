@@ -42,6 +42,7 @@ struct PreParams {
   float* nlse2;              // [B * H * Tq_pad]: -LSE * log2(e), -inf on padding rows
   float* nd;                 // [B * H * Tq_pad]: -D, 0 on padding rows
   float* dq_acc;             // [B * H * Tq, 64]: set to zero
+  unsigned int* next_item;   // work counter of bwd_persistent_kernel: set to zero
 };
 
 // Eight lanes per row, 16-byte loads: a warp covers four rows, a block of 256 threads 32.
@@ -54,6 +55,7 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const PreParams p) 
   const long long bh = prow / p.Tq_pad;
   const int q = static_cast<int>(prow - bh * p.Tq_pad);
   const bool real = prow < p.rows && q < p.Tq;
+  if (prow == 0 && part == 0) *p.next_item = 0u;
   const long long row = bh * p.Tq + q;
   float sum = 0.f;
   if (real) {
@@ -571,6 +573,450 @@ __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const ConvertParams
 }
 
 }  // namespace fused
+
+// ------------------------------------------------------------------ persistent dQ/dK/dV kernel
+// The fused kernel above as a persistent grid: one CTA per SM takes (b, h, 128-key tile) work
+// items from a global counter (heaviest key tiles first, zeroed by bwd_preprocess_kernel) and
+// runs them back to back. Per item the products, the elementwise phases and the dQ reduce are
+// those of bwd_fused_kernel; what changes is what happens between items:
+// * K and V sit in two slots: the TMA warp loads the next item's tiles while the current item
+//   still runs (a slot is refilled once the last dQ product of its previous item has completed
+//   and every role has read that item's index).
+// * The Q / dO ring, S^T, dP^T, P^T, dS and the dQ step keep one step counter across items, so
+//   the first scores of the next item are computed under the last steps of the current one.
+// * The four drain warps write dK and dV (after the item's last dQ step) instead of the
+//   elementwise warps, which go straight on to the next item; the first dV / dK product of the
+//   next item waits for that read (acc_empty).
+// Every wait is bounded, as in the other kernels.
+namespace persist {
+
+using fused::DQ_BOX_ROWS;
+using fused::DQ_WARP0;
+using fused::EW_WARPS;
+using fused::LOAD_WARP;
+using fused::MMA_WARP;
+using fused::SCORE_WARP;
+using fused::STAGES;
+using fused::T;
+using fused::T_DK;
+using fused::T_DPT;
+using fused::T_DQ;
+using fused::T_DV;
+using fused::T_P;
+using fused::T_ST;
+using fused::THREADS;
+using fused::TILE_BYTES;
+using fused::TMEM_COLS;
+
+constexpr int KV_SLOTS = 2;
+
+struct Params {
+  int B, H, Tq, Tk, past_len;
+  int n_k_tiles;
+  int Tq_pad;               // Tq rounded up to whole 128-row tiles
+  int n_items;              // B * H * n_k_tiles
+  const float* nlse2;       // [B, H, Tq_pad]: -LSE * log2(e), -inf on padding rows
+  const float* nd;          // [B, H, Tq_pad]: -D
+  __nv_bfloat16* dk;        // contiguous [B, H, Tk, 64]
+  __nv_bfloat16* dv;
+  unsigned int* next_item;  // work counter, zero at launch
+};
+
+struct alignas(1024) Smem {
+  uint8_t k[KV_SLOTS][TILE_BYTES];
+  uint8_t v[KV_SLOTS][TILE_BYTES];
+  uint8_t q[STAGES][TILE_BYTES];
+  uint8_t dO[STAGES][TILE_BYTES];
+  uint8_t ds[2][T * 128];  // as in bwd_fused_kernel
+  uint8_t dq_stage[4][DQ_BOX_ROWS * 128];
+  float nlse2[STAGES][T];
+  float nd[STAGES][T];
+  volatile int item[KV_SLOTS];  // work item of the slot, -1 once the counter ran out
+  uint64_t kv_full[KV_SLOTS], kv_empty[KV_SLOTS];
+  uint64_t q_full[STAGES], q_empty[STAGES];
+  uint64_t s_full, s_consumed, p_full, pv_free, dp_full, ds_ready, ds_free;
+  uint64_t dq_full, dq_free, acc_final, acc_empty, drain, drain_scores;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "persistent backward shared memory");
+
+// kv_empty of a slot: the commit after the item's last dQ product plus one arrival per drain
+// warp once it has read the item's index (the drain warps are the only role that can still be
+// an item behind when the slot is refilled).
+constexpr int KV_EMPTY_ARRIVALS = 1 + 4;
+
+struct Item {
+  int bh, b, h, k0, qt0, n_q;
+};
+
+__device__ __forceinline__ Item decode_item(const Params& p, int idx) {
+  const int BH = p.B * p.H;
+  Item it;
+  const int kt = idx / BH;  // low key tiles see the most queries: heaviest first
+  it.bh = idx - kt * BH;
+  it.b = it.bh / p.H;
+  it.h = it.bh - it.b * p.H;
+  it.k0 = kt * T;
+  it.qt0 = static_cast<int>(max(0LL, static_cast<long long>(it.k0) - p.past_len) / T);
+  it.n_q = (p.Tq + T - 1) / T - it.qt0;
+  return it;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+bwd_persistent_kernel(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_do,
+                      const __grid_constant__ CUtensorMap tm_dqacc, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < KV_SLOTS; ++i) {
+      mbar_init(&s.kv_full[i], 1);
+      mbar_init(&s.kv_empty[i], KV_EMPTY_ARRIVALS);
+    }
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1);
+    }
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.s_consumed, EW_WARPS);
+    mbar_init(&s.p_full, EW_WARPS);
+    mbar_init(&s.pv_free, 1);
+    mbar_init(&s.dp_full, 1);
+    mbar_init(&s.ds_ready, EW_WARPS);
+    mbar_init(&s.ds_free, 1);
+    mbar_init(&s.dq_full, 1);
+    mbar_init(&s.dq_free, 4);
+    mbar_init(&s.acc_final, 1);
+    mbar_init(&s.acc_empty, 4);
+    mbar_init(&s.drain, 1);
+    mbar_init(&s.drain_scores, 1);
+    s.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == LOAD_WARP) {
+    if (lane == 0) {
+      int items = 0;  // items whose K/V loads were issued
+      int g = 0;      // Q / dO ring loads issued
+      bool ok = true;
+      for (int j = 0; ok; ++j) {
+        const int slot = j & 1;
+        if (j >= KV_SLOTS && !wait_or_abort(s, &s.kv_empty[slot], ((j >> 1) - 1) & 1)) break;
+        const int idx = static_cast<int>(atomicAdd(p.next_item, 1u));
+        if (idx >= p.n_items) {
+          s.item[slot] = -1;
+          mbar_arrive(&s.kv_full[slot]);
+          break;
+        }
+        s.item[slot] = idx;
+        const Item it = decode_item(p, idx);
+        mbar_arrive_expect_tx(&s.kv_full[slot], 2 * TILE_BYTES);
+        tma_load_4d(s.k[slot], &tm_k, &s.kv_full[slot], 0, it.k0, it.h, it.b);
+        tma_load_4d(s.v[slot], &tm_v, &s.kv_full[slot], 0, it.k0, it.h, it.b);
+        items = j + 1;
+        for (int i = 0; i < it.n_q; ++i) {
+          const int st = g % STAGES;
+          if (g >= STAGES && !wait_or_abort(s, &s.q_empty[st], ((g / STAGES) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const int q0 = (it.qt0 + i) * T;
+          const size_t row = static_cast<size_t>(it.bh) * p.Tq_pad + static_cast<size_t>(q0);
+          mbar_arrive_expect_tx(&s.q_full[st], 2 * TILE_BYTES + 2 * T * sizeof(float));
+          tma_load_4d(s.q[st], &tm_q, &s.q_full[st], 0, q0, it.h, it.b);
+          tma_load_4d(s.dO[st], &tm_do, &s.q_full[st], 0, q0, it.h, it.b);
+          bulk_load_plain(s.nlse2[st], p.nlse2 + row, T * sizeof(float), &s.q_full[st]);
+          bulk_load_plain(s.nd[st], p.nd + row, T * sizeof(float), &s.q_full[st]);
+          ++g;
+        }
+      }
+      if (s.abort) {
+        // Let the copies in flight land before the CTA's shared memory is released.
+        for (int j = max(0, items - KV_SLOTS); j < items; ++j)
+          mbar_wait(&s.kv_full[j & 1], (j >> 1) & 1);
+        for (int i = max(0, g - STAGES); i < g; ++i)
+          mbar_wait(&s.q_full[i % STAGES], (i / STAGES) & 1);
+      }
+    }
+  } else if (warp == SCORE_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc_bf16(T, T, false);
+      bool ok = true;
+      int g = 0;
+      for (int j = 0; ok; ++j) {
+        const int slot = j & 1;
+        if (!wait_or_abort(s, &s.kv_full[slot], (j >> 1) & 1)) break;
+        const int idx = s.item[slot];
+        if (idx < 0) break;
+        const Item it = decode_item(p, idx);
+        const uint32_t k_addr = smem_u32(s.k[slot]), v_addr = smem_u32(s.v[slot]);
+        for (int i = 0; i < it.n_q; ++i, ++g) {
+          const int st = g % STAGES;
+          // S^T(g) once the Q tile has landed and the elementwise warps hold S^T(g-1).
+          ok = wait_or_abort(s, &s.q_full[st], (g / STAGES) & 1) &&
+               (g == 0 || wait_or_abort(s, &s.s_consumed, (g - 1) & 1));
+          if (!ok) break;
+          tc_fence_after();
+          issue_scores(tmem + T_ST, k_addr, smem_u32(s.q[st]), idesc_s);
+          umma_commit(&s.s_full);
+          // dP^T(g) overwrites dP^T(g-1): once the elementwise warps have read it.
+          if (g > 0 && !wait_or_abort(s, &s.ds_ready, (g - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_scores(tmem + T_DPT, v_addr, smem_u32(s.dO[st]), idesc_s);
+          umma_commit(&s.dp_full);
+        }
+      }
+      umma_commit(&s.drain_scores);
+      mbar_wait(&s.drain_scores, 0);
+    }
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc_o = make_idesc_bf16(T, HD, true);
+      const uint32_t idesc_dq = make_idesc_bf16(T, HD, true) | (1u << 15);  // A MN-major
+      bool ok = true;
+      int g = 0;
+      for (int j = 0; ok; ++j) {
+        const int slot = j & 1;
+        if (!wait_or_abort(s, &s.kv_full[slot], (j >> 1) & 1)) break;
+        const int idx = s.item[slot];
+        if (idx < 0) break;
+        const Item it = decode_item(p, idx);
+        const uint32_t k_addr = smem_u32(s.k[slot]);
+        for (int i = 0; i < it.n_q; ++i, ++g) {
+          const int st = g % STAGES;
+          ok = wait_or_abort(s, &s.p_full, g & 1) &&
+               // The first products of an item overwrite dV and dK: after the drain warps
+               // have read the previous item's.
+               (i > 0 || j == 0 || wait_or_abort(s, &s.acc_empty, (j - 1) & 1));
+          if (!ok) break;
+          tc_fence_after();
+          fused::issue_dv(tmem + T_DV, tmem + T_P, smem_u32(s.dO[st]), idesc_o, i > 0);
+          umma_commit(&s.pv_free);
+          if (!wait_or_abort(s, &s.ds_ready, g & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          fused::issue_dk(tmem + T_DK, smem_u32(s.ds[0]), smem_u32(s.q[st]), idesc_o, i > 0);
+          // Q(g) and dO(g) were last read by dK(g) and dV(g); S^T(g) and dP^T(g) completed
+          // before the elementwise warps could read them.
+          umma_commit(&s.q_empty[st]);
+          if (i + 1 == it.n_q) umma_commit(&s.acc_final);
+          if (g > 0 && !wait_or_abort(s, &s.dq_free, (g - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          fused::issue_dq(tmem + T_DQ, smem_u32(s.ds[0]), k_addr, idesc_dq);
+          umma_commit(&s.dq_full);
+          umma_commit(&s.ds_free);
+          // K was last read by this dQ product, V by dP^T (complete before dS existed).
+          if (i + 1 == it.n_q) umma_commit(&s.kv_empty[slot]);
+        }
+      }
+      umma_commit(&s.drain);
+      mbar_wait(&s.drain, 0);
+    }
+  } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + 4) {
+    // dQ drain for every step (thread = query row 32 * quarter + lane of the step), then the
+    // item's dK and dV rows (thread = key row 32 * quarter + lane; same TMEM lanes).
+    const int quarter = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t* box = s.dq_stage[quarter];
+    const uint32_t sw = lane & 7;
+    const uint32_t row_addr = smem_u32(box) + lane * 128;
+    bool ok = true;
+    int g = 0;
+    for (int j = 0; ok; ++j) {
+      const int slot = j & 1;
+      if (!warp_wait(s, &s.kv_full[slot], (j >> 1) & 1)) break;
+      const int idx = s.item[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.kv_empty[slot]);
+      if (idx < 0) break;
+      const Item it = decode_item(p, idx);
+      for (int i = 0; i < it.n_q; ++i, ++g) {
+        if (!warp_wait(s, &s.dq_full, g & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t a0[32], a1[32];
+        tmem_ld32(tmem + lane_base + T_DQ, a0);
+        tmem_ld32(tmem + lane_base + T_DQ + 32, a1);
+        tmem_wait_ld();
+        reg_fence(a0);
+        reg_fence(a1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.dq_free);
+          bulk_wait_group_read_all();  // the previous reduce has read the staging box
+        }
+        __syncwarp();
+        const int row0 = (it.qt0 + i) * T + quarter * DQ_BOX_ROWS;
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c)
+          sts_u4(row_addr + ((c ^ sw) << 4), a0[4 * c], a0[4 * c + 1], a0[4 * c + 2], a0[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.Tq) {  // rows past Tq inside a box are clipped by the map
+          tma_reduce_add_4d(box, &tm_dqacc, 0, row0, it.h, it.b);
+          bulk_commit_group();
+          bulk_wait_group_read_all();
+        }
+        __syncwarp();
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c)
+          sts_u4(row_addr + ((c ^ sw) << 4), a1[4 * c], a1[4 * c + 1], a1[4 * c + 2], a1[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.Tq) {
+          tma_reduce_add_4d(box, &tm_dqacc, 32, row0, it.h, it.b);
+          bulk_commit_group();
+        }
+      }
+      if (!ok || !warp_wait(s, &s.acc_final, j & 1)) break;
+      tc_fence_after();
+      const int key = it.k0 + quarter * 32 + lane;
+      const size_t kidx = static_cast<size_t>(it.bh) * p.Tk + static_cast<size_t>(key);
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {  // dK (scaled), then dV
+        uint32_t a0[32], a1[32];
+        tmem_ld32(tmem + lane_base + (part == 0 ? T_DK : T_DV), a0);
+        tmem_ld32(tmem + lane_base + (part == 0 ? T_DK : T_DV) + 32, a1);
+        tmem_wait_ld();
+        reg_fence(a0);
+        reg_fence(a1);
+        if (part == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.acc_empty);
+        }
+        __nv_bfloat16* out = part == 0 ? p.dk : p.dv;
+        const float scale = part == 0 ? SCALE : 1.f;
+        if (key < p.Tk) {
+          store_row_bf16(out + kidx * HD, a0, scale);
+          store_row_bf16(out + kidx * HD + 32, a1, scale);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();
+  } else {
+    // Elementwise warps: thread = key row of the item's tile = TMEM lane; this warp covers
+    // query columns [64 * half, 64 * half + 64) of each step, as in bwd_fused_kernel.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + T_ST + half * 64;
+    const uint32_t t_dp = tmem + lane_base + T_DPT + half * 64;
+    const uint32_t t_p = tmem + lane_base + T_P + half * 32;
+    const uint32_t ds_row = smem_u32(s.ds[half]) + r * 128;
+    const uint32_t sw = static_cast<uint32_t>(r & 7);
+    bool ok = true;
+    int g = 0;
+    for (int j = 0; ok; ++j) {
+      const int slot = j & 1;
+      if (!warp_wait(s, &s.kv_full[slot], (j >> 1) & 1)) break;
+      const int idx = s.item[slot];
+      if (idx < 0) break;
+      const Item it = decode_item(p, idx);
+      const int key = it.k0 + r;
+      for (int i = 0; i < it.n_q; ++i, ++g) {
+        const int st = g % STAGES;
+        const long long q0 = static_cast<long long>(it.qt0 + i) * T;
+        const uint32_t nl_addr = smem_u32(&s.nlse2[st][half * 64]);
+        const uint32_t nd_addr = smem_u32(&s.nd[st][half * 64]);
+        const bool masked = static_cast<long long>(it.k0) + T - 1 > q0 + p.past_len;
+        const int first_visible = static_cast<int>(min(static_cast<long long>(T),
+            max(0LL, key - p.past_len - q0))) - half * 64;
+
+        // Phase 1: P from S^T.
+        if (!warp_wait(s, &s.s_full, g & 1)) { ok = false; break; }
+        tc_fence_after();
+        float pr[64];
+        {
+          uint32_t sr0[32], sr1[32];
+          tmem_ld32(t_s, sr0);
+          tmem_ld32(t_s + 32, sr1);
+          tmem_wait_ld();
+          reg_fence(sr0);
+          reg_fence(sr1);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.s_consumed);
+          // P^T(g - 1) has been read by dV(g - 1).
+          if (g > 0 && !warp_wait(s, &s.pv_free, (g - 1) & 1)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t pk[16];
+          if (masked) fused::ew_probs<true>(sr0, nl_addr, first_visible, pr, pk);
+          else fused::ew_probs<false>(sr0, nl_addr, 0, pr, pk);
+          tmem_st16(t_p, pk);
+          if (masked) fused::ew_probs<true>(sr1, nl_addr + 128, first_visible - 32, pr + 32, pk);
+          else fused::ew_probs<false>(sr1, nl_addr + 128, 0, pr + 32, pk);
+          tmem_st16(t_p + 16, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.p_full);
+
+        // Phase 2: dS from dP^T and the FP32 P, 16 queries at a time.
+        if (!warp_wait(s, &s.dp_full, g & 1)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t dr[16], dsb[8];
+          tmem_ld16(t_dp + 16 * c, dr);
+          tmem_wait_ld();
+          reg_fence16(dr);
+          fused::ew_dscores(pr + 16 * c, dr, nd_addr + 64 * c, dsb);
+          // The dS tile was last read by dK(g - 1) and dQ(g - 1).
+          if (c == 0 && g > 0 && !warp_wait(s, &s.ds_free, (g - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t q8 = 2 * c;  // 8-query chunks q8, q8 + 1 of the half
+          sts_u4(ds_row + ((q8 ^ sw) << 4), dsb[0], dsb[1], dsb[2], dsb[3]);
+          sts_u4(ds_row + (((q8 + 1) ^ sw) << 4), dsb[4], dsb[5], dsb[6], dsb[7]);
+        }
+        if (!ok) break;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.ds_ready);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace persist
 
 }  // namespace backward
 }  // namespace tt

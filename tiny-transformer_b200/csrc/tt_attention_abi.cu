@@ -10,6 +10,7 @@
 #include <climits>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -734,7 +735,20 @@ TT_ATTN_API tt_attn_status tt_qkv_rope_append_bf16(
 
 // Backward workspace: -LSE * log2(e) and -D per query row, each [B, H, Tq_pad] FP32 with Tq
 // padded to whole 128-row tiles (so every tile's rows are one aligned 512-byte copy), then the
-// FP32 dQ accumulator [B, H, Tq, 64] that the fused kernel reduces into.
+// FP32 dQ accumulator [B, H, Tq, 64] that the fused kernel reduces into, then the persistent
+// kernel's work counter (16 bytes, keeping the total a multiple of 16).
+constexpr size_t kBackwardCounterBytes = 16;
+
+// The persistent backward kernel is selected by TT_ATTN_BWD_PERSISTENT=1 in the environment
+// (read once per process); bwd_fused_kernel is the default.
+bool use_persistent_backward() {
+  static const bool on = [] {
+    const char* v = std::getenv("TT_ATTN_BWD_PERSISTENT");
+    return v != nullptr && v[0] == '1' && v[1] == '\0';
+  }();
+  return on;
+}
+
 int64_t backward_q_pad(int64_t q_len) {
   const int64_t t = tt::backward::fused::T;
   return (q_len + t - 1) / t * t;
@@ -745,7 +759,8 @@ TT_ATTN_API size_t tt_attn_backward_workspace_size(int64_t batch, int64_t heads,
     return 0;
   const int64_t bh = batch * heads;
   return 2 * static_cast<size_t>(bh * backward_q_pad(q_len)) * sizeof(float) +
-         static_cast<size_t>(bh * q_len) * TT_ATTN_HEAD_DIM * sizeof(float);
+         static_cast<size_t>(bh * q_len) * TT_ATTN_HEAD_DIM * sizeof(float) +
+         kBackwardCounterBytes;
 }
 
 }  // extern "C"
@@ -862,8 +877,8 @@ tt_attn_status backward_impl(
     return fail(TT_ATTN_BAD_ARG, "workspace is smaller than tt_attn_backward_workspace_size() "
                                  "or not 16-byte aligned");
 
-  int dev = 0;
-  tt_attn_status st = prepare_device(&dev);
+  int dev = 0, sm_count = 0;
+  tt_attn_status st = prepare_device(&dev, &sm_count);
   if (st != TT_ATTN_OK) return st;
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
   const int64_t cstr[4] = {heads * q_len * TT_ATTN_HEAD_DIM, q_len * TT_ATTN_HEAD_DIM,
@@ -875,6 +890,7 @@ tt_attn_status backward_impl(
   float* nlse2 = static_cast<float*>(workspace);
   float* nd = nlse2 + pad_rows;
   float* dq_acc = nd + pad_rows;
+  unsigned int* next_item = reinterpret_cast<unsigned int*>(dq_acc + rows * TT_ATTN_HEAD_DIM);
 
   constexpr unsigned tile = tt::backward::fused::T;
   CUtensorMap tmq, tmdo, tmk, tmv, tmacc;
@@ -894,11 +910,40 @@ tt_attn_status backward_impl(
   pp.nlse2 = nlse2;
   pp.nd = nd;
   pp.dq_acc = dq_acc;
+  pp.next_item = next_item;
   const int64_t pre_blocks =
       (pad_rows + tt::backward::PRE_ROWS_PER_BLOCK - 1) / tt::backward::PRE_ROWS_PER_BLOCK;
   tt::backward::bwd_preprocess_kernel<<<static_cast<unsigned>(pre_blocks), 256, 0, cs>>>(pp);
   if ((st = check_launch("bwd_preprocess_kernel launch")) != TT_ATTN_OK) return st;
 
+  if (use_persistent_backward()) {
+    tt::backward::persist::Params pq{};
+    pq.B = static_cast<int>(batch);
+    pq.H = static_cast<int>(heads);
+    pq.Tq = static_cast<int>(q_len);
+    pq.Tk = static_cast<int>(kv_len);
+    pq.past_len = static_cast<int>(past_len);
+    pq.n_k_tiles = static_cast<int>(k_tiles);
+    pq.Tq_pad = static_cast<int>(q_pad);
+    pq.n_items = static_cast<int>(bh * k_tiles);
+    pq.nlse2 = nlse2;
+    pq.nd = nd;
+    pq.dk = static_cast<__nv_bfloat16*>(dk);
+    pq.dv = static_cast<__nv_bfloat16*>(dv);
+    pq.next_item = next_item;
+    const int64_t grid = std::min<int64_t>(bh * k_tiles, sm_count > 0 ? sm_count : 148);
+    const cudaError_t ae = cudaFuncSetAttribute(tt::backward::persist::bwd_persistent_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(tt::backward::persist::kSmemBytes));
+    if (ae != cudaSuccess)
+      return fail(TT_ATTN_LAUNCH_FAIL,
+                  std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ae));
+    tt::backward::persist::bwd_persistent_kernel<<<static_cast<unsigned>(grid),
+                                                   tt::backward::persist::THREADS,
+                                                   tt::backward::persist::kSmemBytes, cs>>>(
+        tmq, tmk, tmv, tmdo, tmacc, pq);
+    if ((st = check_launch("bwd_persistent_kernel launch")) != TT_ATTN_OK) return st;
+  } else {
   tt::backward::fused::Params p{};
   p.B = static_cast<int>(batch);
   p.H = static_cast<int>(heads);
@@ -916,6 +961,7 @@ tt_attn_status backward_impl(
                                           tt::backward::fused::kSmemBytes, cs>>>(
       tmq, tmk, tmv, tmdo, tmacc, p);
   if ((st = check_launch("bwd_fused_kernel launch")) != TT_ATTN_OK) return st;
+  }
 
   tt::backward::fused::ConvertParams cp{};
   cp.rows = rows;
