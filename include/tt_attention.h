@@ -123,8 +123,8 @@ TT_ATTN_API tt_attn_status tt_attn_device_status(unsigned* flags, int clear);
  *               the FP32 dQ accumulator and a work counter; its contents on entry do not matter)
  *
  * Mask: key j visible to query i iff j <= i + past_len, kv_len == q_len + past_len.
- * On `stream`, in order, three kernels: row sums D (which also zeroes the dQ accumulator), one
- * fused dQ/dK/dV kernel, dQ scaling to bf16. Nothing is allocated.
+ * On `stream`, in order, three kernels: row sums D (which also zeroes the dQ accumulator and
+ * the work counter), one persistent dQ/dK/dV kernel, dQ scaling to bf16. Nothing is allocated.
  */
 TT_ATTN_API tt_attn_status tt_attn_backward_bf16(
     const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,

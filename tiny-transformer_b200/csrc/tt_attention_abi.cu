@@ -739,12 +739,12 @@ TT_ATTN_API tt_attn_status tt_qkv_rope_append_bf16(
 // kernel's work counter (16 bytes, keeping the total a multiple of 16).
 constexpr size_t kBackwardCounterBytes = 16;
 
-// The persistent backward kernel is selected by TT_ATTN_BWD_PERSISTENT=1 in the environment
-// (read once per process); bwd_fused_kernel is the default.
+// bwd_persistent_kernel is the default; TT_ATTN_BWD_PERSISTENT=0 in the environment (read once
+// per process) selects the one-CTA-per-key-tile bwd_fused_kernel instead.
 bool use_persistent_backward() {
   static const bool on = [] {
     const char* v = std::getenv("TT_ATTN_BWD_PERSISTENT");
-    return v != nullptr && v[0] == '1' && v[1] == '\0';
+    return !(v != nullptr && v[0] == '0' && v[1] == '\0');
   }();
   return on;
 }
