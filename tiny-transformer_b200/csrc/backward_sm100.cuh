@@ -12,9 +12,11 @@
 // Three kernels, in stream order:
 // * bwd_preprocess_kernel: -D and -LSE * log2(e) per query row, in rows padded to whole
 //   128-row tiles (eight lanes per row, 16-byte loads of dO and O), and zeros for the row's
-//   FP32 dQ accumulator (the same pass instead of a separate memset).
-// * fused::bwd_fused_kernel: one CTA per (b, h, 128-key tile); S, dP and the exponentials are
-//   computed once per (query tile, key tile) pair and feed dV, dK and dQ (see below).
+//   FP32 dQ accumulator (the same pass instead of a separate memset), plus the work counter of
+//   the persistent kernel.
+// * persist::bwd_persistent_kernel (default): one CTA per SM running (b, h, 128-key tile) items
+//   back to back, or fused::bwd_fused_kernel: one CTA per item. Either way S, dP and the
+//   exponentials are computed once per (query tile, key tile) pair and feed dV, dK and dQ.
 // * fused::bwd_dq_convert_kernel: dQ = bf16(scale * dQ accumulator).
 // Every mbarrier wait is bounded (TT_ERR_TIMEOUT + abort flag), as in the forward kernels.
 #pragma once
