@@ -719,12 +719,14 @@ bwd_persistent_kernel(const __grid_constant__ CUtensorMap tm_q,
       for (int j = 0; ok; ++j) {
         const int slot = j & 1;
         if (j >= KV_SLOTS && !wait_or_abort(s, &s.kv_empty[slot], ((j >> 1) - 1) & 1)) break;
-        const int idx = static_cast<int>(atomicAdd(p.next_item, 1u));
-        if (idx >= p.n_items) {
+        // Compared unsigned: the counter passes n_items by up to one grab per CTA.
+        const unsigned int grab = atomicAdd(p.next_item, 1u);
+        if (grab >= static_cast<unsigned int>(p.n_items)) {
           s.item[slot] = -1;
           mbar_arrive(&s.kv_full[slot]);
           break;
         }
+        const int idx = static_cast<int>(grab);
         s.item[slot] = idx;
         const Item it = decode_item(p, idx);
         mbar_arrive_expect_tx(&s.kv_full[slot], 2 * TILE_BYTES);
