@@ -68,7 +68,10 @@ class Res:
 class Sim:
     # Protocol switches; the defaults are the kernel's protocol, the others plant mistakes.
     def __init__(self, items, seed, drain_releases_slot=True, wait_acc_empty=True,
-                 dp_waits_ds_ready=True, q_empty_by_accumulate=True):
+                 dp_waits_ds_ready=True, q_empty_by_accumulate=True, epilogue_first=False):
+        # epilogue_first: the drain warps read an item's dK/dV before draining its last dQ step
+        # (an ordering the kernel could adopt; checked here ahead of any change to it).
+        self.epilogue_first = epilogue_first
         self.drain_releases_slot = drain_releases_slot
         self.wait_acc_empty = wait_acc_empty
         self.dp_waits_ds_ready = dp_waits_ds_ready
@@ -235,15 +238,22 @@ class Sim:
                 self.bars[f"kv_empty{slot}"].arrive(self)
             if idx < 0:
                 return
-            for i in range(self.items[idx]):
+            n = self.items[idx]
+            for i in range(n):
+                if i + 1 == n and self.epilogue_first:
+                    yield from self.epilogue(j)
                 yield ("wait", "dq_full", g)
                 self.res["DQ"].read(g)
                 self.bars["dq_free"].arrive(self)
                 g += 1
-            yield ("wait", "acc_final", j)
-            self.res["ACC"].read(("fin", j))
-            self.bars["acc_empty"].arrive(self)
+            if not self.epilogue_first:
+                yield from self.epilogue(j)
             j += 1
+
+    def epilogue(self, j):
+        yield ("wait", "acc_final", j)
+        self.res["ACC"].read(("fin", j))
+        self.bars["acc_empty"].arrive(self)
 
     def ew(self, w):
         g = 0
@@ -335,9 +345,10 @@ def random_items(seed):
     return [rng.randint(1, 5) for _ in range(rng.randint(0, 7))]
 
 
-def test_protocol_random_interleavings():
+@pytest.mark.parametrize("epilogue_first", [False, True])
+def test_protocol_random_interleavings(epilogue_first):
     for seed in range(2000):
-        Sim(random_items(seed), seed).run()
+        Sim(random_items(seed), seed, epilogue_first=epilogue_first).run()
 
 
 @pytest.mark.parametrize("mistake, message", [
