@@ -145,8 +145,8 @@ class deterministic_algorithms:
 @torch.no_grad()
 def test_bf16_native_backward_is_deterministic_and_leaves_inputs(ext):
     """Deterministic mode (like the reference's atomic-free kernels): bit-identical repeats. The
-    default fused path adds dQ contributions in timing-dependent order: dK and dV (one CTA per
-    key tile, fixed order) still repeat exactly, dQ within one bf16 ulp."""
+    default path adds dQ contributions in timing-dependent order: dK and dV (each key tile's
+    from one CTA, in a fixed order) still repeat exactly, dQ within one bf16 ulp."""
     torch.manual_seed(7)
     q, k, v = [torch.randn(3, 4, t, 64, device="cuda", dtype=torch.bfloat16) for t in (300, 300, 300)]
     out, lse = ext.attention_forward(q, k, v)
